@@ -1,0 +1,105 @@
+/* tempo_sm100.h -- C-ABI of the sm_100a (B200) GEMM backend of the tempolator.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as void*,
+ * and returns an int that is a cudaError_t value.  Semantics follow the reference's shipped
+ * POD ABI (kernels/shipped/gemm_fp16/sm_70/launch.cuh:20-75, launch.cu:20-22,
+ * dispatch.inc:15-26):
+ *
+ *   0  (cudaSuccess)                    the kernel was launched on `stream`
+ *   9  (cudaErrorInvalidConfiguration)  "not covered": the caller must take its own fallback
+ *                                       path (F.linear / cuBLAS), exactly like the reference
+ *                                       dispatcher's last line (dispatch.inc:26)
+ *   other                               a real CUDA error
+ *
+ * Layouts (the reference's k/k/n layout, kernels/naive/gemm_fp16.cu:16-38):
+ *   A [M][K] fp16, row stride lda;   B [N][K] fp16, row stride ldb;   C [M][N] fp16, ldc.
+ *   C = A * B^T with fp32 accumulation.  Strides are in elements and must be multiples of
+ *   8 (16 bytes); base pointers 16-byte aligned; K and N multiples of 8.
+ *
+ * Workspace: split-K launches need `ws` (device memory, zero-filled once by the caller before
+ * its first use; every launch leaves it zero-filled again).  Query the size with
+ * tempo_sm100_workspace_bytes.  ws == NULL or too small is legal: the dispatcher then picks
+ * a configuration without split-K.  One workspace must not be shared by launches that can
+ * run concurrently (different streams).
+ *
+ * Threading: all entry points are re-entrant; per-device one-time set-up is internal.
+ */
+#ifndef TEMPO_SM100_H
+#define TEMPO_SM100_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight quantisation kinds for the W8A16 op. */
+#define TEMPO_W8_INT8_PER_CHANNEL 1  /* int8 W [N][K], fp16 scale [N]; W = q * s[n]           */
+#define TEMPO_W8_UINT8_GROUP 2       /* uint8 W [N][K], fp16 scale/uint8 zero [N][K/g];
+                                        W = (q - z[n][k/g]) * s[n][k/g]                     */
+
+/* Replaces tempo::gen::applicable(const GemmParams&) (launch.cuh:59-67).  1 = covered. */
+int tempo_sm100_gemm_fp16_applicable(const void* A, const void* B, const void* C, int M, int N,
+                                     int K, int lda, int ldb, int ldc);
+
+/* Replaces tempo::gen::launch(const GemmParams&, cudaStream_t) (launch.cuh:75, launch.cu:20-22):
+ * C[M][N] = A[M][K] * B[N][K]^T, fp16 in/out, fp32 accumulate, tcgen05 tensor cores. */
+int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, int lda,
+                          int ldb, int ldc, void* ws, size_t ws_bytes, void* stream);
+
+/* The W8A16 op (north-star skeleton gemm_w8a16; the reference's unshipped sm70 skeleton is
+ * tempo/plugins/sm70/skeletons/gemm_w8a16/kernel.cuh:226-296, its GPTQ reconstruction formula
+ * bench/gemm_baseline.py:214-231).  W is [N][K] 8-bit, row stride ldw (bytes, multiple of 16).
+ * quant_kind TEMPO_W8_INT8_PER_CHANNEL: scale [N], zero ignored, group_size ignored.
+ * quant_kind TEMPO_W8_UINT8_GROUP: scale fp16 [N][K/group_size], zero uint8 [N][K/group_size],
+ * group_size a multiple of 64 dividing K. */
+int tempo_sm100_gemm_w8a16_applicable(const void* A, const void* W, const void* scale,
+                                      const void* zero, const void* C, int M, int N, int K,
+                                      int lda, int ldw, int ldc, int quant_kind, int group_size);
+int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, const void* zero,
+                           void* C, int M, int N, int K, int lda, int ldw, int ldc, int quant_kind,
+                           int group_size, void* ws, size_t ws_bytes, void* stream);
+
+/* Workspace bytes the dispatcher would like for this problem (0 = no split-K wanted).
+ * weight_kind: 0 = fp16, else a TEMPO_W8_* kind. */
+size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind);
+
+/* One explicit hyperform (the plugin's search axes; used by the build/measure stages and the
+ * tuner).  bn: MMA N tile (16..256), swap: 1 = weights on the 128-row MMA side, splits: k-split
+ * count (1 = none), group_m: raster group height in 128-row tiles, max_ctas: persistent grid
+ * cap (0 = one CTA per SM).  Returns 9 if the hyperform is not instantiated or does not fit. */
+int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, const void* scale,
+                               const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                               int ldc, int group_size, int bn, int swap, int splits, int group_m,
+                               int max_ctas, void* ws, size_t ws_bytes, void* stream);
+
+/* The dispatcher's choice for a problem: out[0..4] = bn, swap, splits, group_m, stages.
+ * Returns 9 if the problem is not covered. */
+int tempo_sm100_select(int weight_kind, int M, int N, int K, size_t ws_bytes, int* out5);
+
+/* Resource facts of one instantiation: out[0..5] = threads, dynamic smem bytes, stages,
+ * TMEM columns, registers per thread, local (stack/spill) bytes per thread.  Non-zero return
+ * if the instantiation does not exist. */
+int tempo_sm100_hyperform_resources(int weight_kind, int bn, int swap, int* out6);
+
+/* The naive INPUT bar (one thread per output, fp32 accumulate) -- the reference's
+ * kernels/naive/gemm_fp16.cu:60-76 operation, and its W8A16 analogue. */
+int tempo_sm100_naive_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K,
+                                int lda, int ldb, int ldc, void* stream);
+int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale,
+                                 const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                                 int ldc, int quant_kind, int group_size, void* stream);
+
+/* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
+ * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the
+ * current device. */
+int tempo_sm100_device_status(int* out4, int reset);
+
+/* Library identification string. */
+const char* tempo_sm100_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TEMPO_SM100_H */

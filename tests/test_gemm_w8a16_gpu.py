@@ -1,0 +1,75 @@
+"""GPU parity of the W8A16 tcgen05 GEMM (smem dequant) against the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import gemm_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = O.GATE_REL_L2
+
+
+def _pc(M, N, K, fn, seed=2):
+    a, q, s = O.inputs_w8_per_channel(M, N, K, seed)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    C.view(torch.int16).fill_(0x7F7F)
+    fn(torch.from_numpy(a).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), C)
+    torch.cuda.synchronize()
+    c = C.cpu().numpy()
+    assert O.poison_count(c) == 0
+    ref = O.gemm_w_ref(a, O.dequant_per_channel(q, s))
+    return O.rel_l2(c, ref)
+
+
+def _grp(M, N, K, fn, G=128, seed=3):
+    a, q, s, z = O.inputs_w8_group(M, N, K, G, seed)
+    C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    C.view(torch.int16).fill_(0x7F7F)
+    fn(torch.from_numpy(a).cuda(), torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(),
+       torch.from_numpy(z).cuda(), G, C)
+    torch.cuda.synchronize()
+    c = C.cpu().numpy()
+    assert O.poison_count(c) == 0
+    ref = O.gemm_w_ref(a, O.dequant_group(q, s, z, G))
+    return O.rel_l2(c, ref)
+
+
+SHAPES = [(1, 136, 256), (5, 520, 1024), (16, 1024, 512), (64, 264, 384), (200, 776, 1024),
+          (512, 1040, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_per_channel_dispatch(dev, M, N, K):
+    from cuda_tempiler_b200 import ops
+    r = _pc(M, N, K, lambda A, W, s, C: ops.gemm_w8a16(A, W, s, out=C))
+    assert r <= TOL, r
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_group_dispatch(dev, M, N, K):
+    from cuda_tempiler_b200 import ops
+    r = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_w8a16(A, W, s, z, G, out=C))
+    assert r <= TOL, r
+
+
+HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, False), (256, False)]
+
+
+@pytest.mark.parametrize("bn,swap", HYPER)
+@pytest.mark.parametrize("splits", [1, 2])
+def test_every_hyperform(dev, bn, swap, splits):
+    from cuda_tempiler_b200 import ops
+    M = 24 if swap else 260
+    r1 = _pc(M, 776, 1024, lambda A, W, s, C: ops.gemm_hyperform(
+        A, W, bn=bn, swap=swap, splits=splits, scale=s, out=C))
+    r2 = _grp(M, 776, 1024, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+        A, W, bn=bn, swap=swap, splits=splits, scale=s, zero=z, group_size=G, out=C))
+    assert r1 <= TOL and r2 <= TOL, (r1, r2)
+
+
+def test_naive_w8(dev):
+    from cuda_tempiler_b200 import ops
+    r = _pc(40, 136, 256, lambda A, W, s, C: C.copy_(ops.naive_gemm_w8a16(A, W, s)))
+    assert r <= TOL
+    r = _grp(40, 136, 256, lambda A, W, s, z, G, C: C.copy_(ops.naive_gemm_w8a16(A, W, s, z, G)))
+    assert r <= TOL
