@@ -1,0 +1,481 @@
+#!/usr/bin/env python3
+"""bench.py -- the driver's benchmark contract for the sm_100a GEMM path.
+
+Workload (one "step"): BASELINE config 2, the fp16 transformer-layer GEMM set -- qkv
+8192x3840, o_proj 3840x4096, gate_up 30720x3840, down 3840x15360, each at M in
+{1, 16, 128, 1024, 4096}: 20 GEMMs C = A * W^T (fp16 in/out, fp32 accumulate) per step.
+Weights N(0, 0.02), activations N(0, 1), seeded synthetic (no checkpoints).
+
+  value      whole-job TFLOP/s (sum of 2MNK over the step / device time per step),
+             inputs resident in HBM; max over ranks; N > 1 runs independent replicas
+             ("replicas only": a standalone GEMM has no exchange step).
+  e2e        the same metric through the C-ABI entry point with HOST buffers: every step
+             copies each GEMM's activations from pinned host memory and reads every C back.
+  roofline   of the dominant kernel (largest share of the step), CUDA-event timed.
+  per_gemm   per shape x M: TFLOP/s, GB/s, bound, fraction of the measured roofline,
+             x cuBLAS (torch F.linear on the same inputs) and x naive INPUT (M <= 128).
+  cpu_baseline  fp32 numpy matmul (the reference's CPU path) on a bounded sample, rank 0.
+
+L2: every step streams 448 MB of distinct weights and consecutive GEMMs use different weight
+matrices, so no weight is L2-resident when it is used again (inputs larger than L2).
+
+``--impl reference`` times the reference's CPU path (fp32 numpy matmul on the host cores,
+through oracle/): each step is one GEMM of the set, cycling in order.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "TFLOP/s & HBM GB/s per GEMM shape vs cuBLAS, % of roofline, 1/2/4/8 GPU"
+UNIT = "TFLOP/s"
+WORKLOAD = "config2: fp16 transformer-layer GEMM set (qkv, o_proj, gate_up, down) x M{1,16,128,1024,4096}"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-bars", action="store_true", help="skip cuBLAS/naive/CPU side measurements")
+    ap.add_argument("--case", default=None,
+                    help="profiling case NAME:M[:kind] (e.g. gate_up:4096, gate_up:1:w8pc): launch "
+                         "that one GEMM warmup+steps times and print its event timing")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm=d["hbm_gbs"], tc=d["bf16_tflops"], tc_sus=d["bf16_tflops_sustained"],
+                    src="measured")
+    return dict(hbm=6650.0, tc=1590.0, tc_sus=1400.0, src="fallback")
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 100 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ------------------------------------------------------------------------------ reference arm
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from cuda_tempiler_b200 import workloads as WL
+    from oracle import gemm_oracle as O
+
+    rng = np.random.default_rng(1)
+    # order: every 5 consecutive steps cover all five M values of one shape, so any prefix
+    # of the cycle has the set's M mix
+    gemms = []
+    for s in WL.LAYER_FP16:
+        for M in WL.LAYER_FP16_M:
+            gemms.append((s.name, M, s.N, s.K))
+    weights = {}
+    for s in WL.LAYER_FP16:  # fp32 upcast once, outside every timer
+        weights[s.name] = (rng.standard_normal((s.N, s.K), dtype=np.float32) * 0.02).astype(
+            np.float16).astype(np.float32)
+    acts = {}
+    for name, M, N, K in gemms:
+        acts[(name, M)] = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
+
+    def step(i):
+        name, M, N, K = gemms[i % len(gemms)]
+        O.gemm_w_ref(acts[(name, M)], weights[name])
+        return 2 * M * N * K
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    flops = 0
+    for i in range(args.steps):
+        flops += step(i)
+    dt = time.perf_counter() - t0
+    v = flops / dt / 1e12
+    cores = os.cpu_count()
+    sample = (f"{args.steps} steps, each one GEMM of the config-2 set, cycling shape-major over M "
+              f"(fp32 numpy matmul, OpenBLAS, {cores} host threads)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+        "config": {"workload": WORKLOAD, "l2": "inputs larger than L2", "host": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------ profiling case
+def run_case(args):
+    """One GEMM of the BASELINE sets, launched warmup + steps times (the ncu capture target)."""
+    import torch
+
+    from cuda_tempiler_b200 import ops
+    from cuda_tempiler_b200 import workloads as WL
+
+    parts = args.case.split(":")
+    name, M = parts[0], int(parts[1])
+    kind = parts[2] if len(parts) > 2 else "fp16"
+    table = WL.LAYER_FP16 if kind == "fp16" else WL.LAYER_W8
+    shape = next(s for s in table if s.name == name)
+    N, K = shape.N, shape.K
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    A = torch.randn(M, K, generator=g, device=dev).half()
+    if kind == "fp16":
+        W = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+        f = lambda: ops.gemm_fp16(A, W)
+        by = WL.algorithmic_bytes(M, N, K)
+    elif kind == "w8pc":
+        W = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+        s = (torch.rand(N, generator=g, device=dev) * 1e-3 + 1e-4).half()
+        f = lambda: ops.gemm_w8a16(A, W, s)
+        by = WL.algorithmic_bytes(M, N, K, 1, "per_channel")
+    else:
+        G = WL.W8_GROUP_SIZE
+        W = torch.randint(0, 256, (N, K), generator=g, device=dev, dtype=torch.uint8)
+        s = (torch.rand(N, K // G, generator=g, device=dev) * 0.019 + 1e-3).half()
+        z = torch.randint(100, 157, (N, K // G), generator=g, device=dev, dtype=torch.uint8)
+        f = lambda: ops.gemm_w8a16(A, W, s, z, G)
+        by = WL.algorithmic_bytes(M, N, K, 1, "group", G)
+    for _ in range(args.warmup):
+        f()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        f()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / args.steps * 1e-3
+    print(json.dumps({"case": args.case, "us": t * 1e6, "tflops": WL.flops(M, N, K) / t / 1e12,
+                      "gbs": by / t / 1e9, "cfg": ops.select(0 if kind == "fp16" else
+                                                             (1 if kind == "w8pc" else 2), M, N, K)}))
+    return 0
+
+
+# ------------------------------------------------------------------------------ our arm
+def main():
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if args.case:
+        return run_case(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from cuda_tempiler_b200 import _lib, ops
+    from cuda_tempiler_b200 import workloads as WL
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    gemms = []
+    weights = {}
+    for s in WL.LAYER_FP16:
+        weights[s.name] = (torch.randn(s.N, s.K, generator=g, device=dev) * 0.02).half()
+    for M in WL.LAYER_FP16_M:
+        for s in WL.LAYER_FP16:
+            A = torch.randn(M, s.K, generator=g, device=dev).half()
+            Cm = torch.empty(M, s.N, dtype=torch.float16, device=dev)
+            gemms.append(dict(name=s.name, M=M, N=s.N, K=s.K, A=A, W=weights[s.name], C=Cm))
+    ws_bytes = max(lib.tempo_sm100_workspace_bytes(x["M"], x["N"], x["K"], 0) for x in gemms)
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    fn = lib.tempo_sm100_gemm_fp16
+    calls = []
+    for x in gemms:
+        calls.append((x["A"].data_ptr(), x["W"].data_ptr(), x["C"].data_ptr(), x["M"], x["N"],
+                      x["K"], x["K"], x["K"], x["N"], ws.data_ptr(), ws.numel(), sh))
+
+    def run_gemm(i):
+        rc = fn(*calls[i])
+        if rc:
+            raise RuntimeError(f"tempo_sm100_gemm_fp16 rc={rc} on {gemms[i]['name']} M={gemms[i]['M']}")
+
+    n = len(gemms)
+    flops_step = sum(WL.flops(x["M"], x["N"], x["K"]) for x in gemms)
+
+    # ---- warm-up (W >= 3 untimed steps)
+    for _ in range(max(args.warmup, 3)):
+        for i in range(n):
+            run_gemm(i)
+    torch.cuda.synchronize()
+
+    # ---- timed region: exactly K steps, per-GEMM events inside, barrier + sync both sides
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)] for _ in range(min(args.steps, 50))]
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        evk = ev[k] if k < len(ev) else None
+        for i in range(n):
+            if evk:
+                evk[i][0].record(stream)
+            run_gemm(i)
+            if evk:
+                evk[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_total = t_start.elapsed_time(t_end)
+    if world > 1:
+        tt = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms_total = float(tt.item())
+    ms_step = ms_total / args.steps
+    value = flops_step * world / (ms_step * 1e-3) / 1e12
+    per_ms = [statistics.median(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(len(ev)))
+              for i in range(n)]
+    status = ops.device_status(reset=True)
+    if status[0] != 0:
+        raise RuntimeError(f"device status {status}: a bounded wait timed out")
+
+    # ---- end to end through the C-ABI with host buffers (pinned), copies inside the timer
+    host_A = [x["A"].cpu().pin_memory() for x in gemms]
+    host_C = [torch.empty(x["C"].shape, dtype=torch.float16).pin_memory() for x in gemms]
+    h2d = sum(t.numel() * 2 for t in host_A)
+    d2h = sum(t.numel() * 2 for t in host_C)
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for i, x in enumerate(gemms):
+            x["A"].copy_(host_A[i], non_blocking=True)
+            run_gemm(i)
+            host_C[i].copy_(x["C"], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = flops_step * world / (e2e_ms * 1e-3) / 1e12
+
+    # ---- per-GEMM bars: cuBLAS (torch F.linear) and the naive INPUT kernel (M <= 128)
+    peaks = load_peaks()
+    per_gemm = []
+    cublas_ms = [None] * n
+    naive_ms = [None] * n
+    if not args.no_bars:
+        def t_of(f, reps):
+            es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
+            for a, b in es:
+                a.record(stream)
+                f()
+                b.record(stream)
+            torch.cuda.synchronize()
+            return statistics.median(a.elapsed_time(b) for a, b in es)
+
+        F = torch.nn.functional
+        for _ in range(2):
+            for x in gemms:
+                F.linear(x["A"], x["W"])
+        torch.cuda.synchronize()
+        # interleave in the same order as the timed step so L2 state matches
+        reps = 10
+        samples = [[] for _ in range(n)]
+        for _ in range(reps):
+            for i, x in enumerate(gemms):
+                samples[i].append(t_of(lambda: F.linear(x["A"], x["W"]), 1))
+        cublas_ms = [statistics.median(s) for s in samples]
+        for i, x in enumerate(gemms):
+            if x["M"] <= 128:
+                naive_ms[i] = t_of(lambda: ops.naive_gemm_fp16(x["A"], x["W"]), 2)
+    for i, x in enumerate(gemms):
+        M, N, K = x["M"], x["N"], x["K"]
+        t = per_ms[i] * 1e-3
+        fl = WL.flops(M, N, K)
+        by = WL.algorithmic_bytes(M, N, K)
+        tflops = fl / t / 1e12
+        gbs = by / t / 1e9
+        t_floor = max(fl / (peaks["tc_sus"] * 1e12), by / (peaks["hbm"] * 1e9))
+        bound = "tensor" if fl / (peaks["tc_sus"] * 1e12) >= by / (peaks["hbm"] * 1e9) else "hbm"
+        per_gemm.append({
+            "gemm": x["name"], "M": M, "N": N, "K": K, "us": round(per_ms[i] * 1e3, 2),
+            "tflops": round(tflops, 1), "gbs": round(gbs, 0), "bound": bound,
+            "roofline_frac": round(t_floor / t, 3),
+            "x_cublas": round(cublas_ms[i] / per_ms[i], 3) if cublas_ms[i] else None,
+            "x_naive": round(naive_ms[i] / per_ms[i], 1) if naive_ms[i] else None,
+            "cfg": ops.select(0, M, N, K, ws.numel()),
+        })
+
+    # ---- roofline of the dominant kernel
+    dom = max(range(n), key=lambda i: per_ms[i])
+    x = gemms[dom]
+    fl = WL.flops(x["M"], x["N"], x["K"])
+    by = WL.algorithmic_bytes(x["M"], x["N"], x["K"])
+    t = per_ms[dom] * 1e-3
+    traffic = load_traffic().get(f"{x['name']}_M{x['M']}")
+    if fl / (peaks["tc_sus"] * 1e12) >= by / (peaks["hbm"] * 1e9):
+        roof = {"bound": "tensor", "achieved": fl / t / 1e12, "peak": peaks["tc_sus"],
+                "unit": "TFLOP/s", "kernel": f"{x['name']} M={x['M']} N={x['N']} K={x['K']}",
+                "algorithmic": f"2MNK = {fl} FLOP per launch",
+                "peak_source": f"{peaks['src']} bf16_tflops_sustained (kernel timed inside a long step)"}
+    else:
+        roof = {"bound": "hbm", "achieved": by / t / 1e9, "peak": peaks["hbm"], "unit": "GB/s",
+                "kernel": f"{x['name']} M={x['M']}", "algorithmic": f"{by} bytes per launch",
+                "peak_source": f"{peaks['src']} hbm_gbs"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = traffic
+    roof["share_of_step"] = per_ms[dom] / sum(per_ms)
+
+    # ---- CPU baseline (rank 0, N = 1): fp32 numpy matmul on a bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_bars:
+        import numpy as np
+
+        from oracle import gemm_oracle as O
+        sample_ix = [i for i, x in enumerate(gemms) if x["M"] <= 1024]
+        w32 = {k: v.float().cpu().numpy() for k, v in weights.items()}
+        a16 = {i: gemms[i]["A"].cpu().numpy() for i in sample_ix}
+        O.gemm_w_ref(a16[sample_ix[0]], w32[gemms[sample_ix[0]]["name"]])
+        t0 = time.perf_counter()
+        cf = 0
+        for i in sample_ix:
+            O.gemm_w_ref(a16[i], w32[gemms[i]["name"]])
+            cf += WL.flops(gemms[i]["M"], gemms[i]["N"], gemms[i]["K"])
+        dt = time.perf_counter() - t0
+        cpu = {"value": cf / dt / 1e12, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+               "sample": f"the 16 GEMMs of the set with M <= 1024 once ({cf/1e9:.0f} GFLOP, "
+                         f"{dt:.1f} s), fp32 numpy/OpenBLAS on {os.cpu_count()} host threads"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16 activations, N(0,0.02) fp16 weights)",
+        "config": {"workload": WORKLOAD, "gemms_per_step": n,
+                   "l2": "inputs larger than L2 (448 MB of distinct weights per step; "
+                         "consecutive GEMMs use different weights)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "accumulate": "fp32"},
+        "clocks": clk,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "tempo_sm100_gemm_fp16 via ctypes; pinned host A in, C out, weights resident"},
+        "gpu_launches": n * args.steps,
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "per_gemm": per_gemm,
+        "x_cublas_median": statistics.median(p["x_cublas"] for p in per_gemm) if per_gemm and per_gemm[0]["x_cublas"] else None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
