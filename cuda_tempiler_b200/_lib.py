@@ -18,6 +18,7 @@ CUDA_ERROR_INVALID_CONFIGURATION = 9  # "not covered": caller takes its fallback
 
 W8_INT8_PER_CHANNEL = 1
 W8_UINT8_GROUP = 2
+NOALLOC_SCRATCH_BYTES = 64 * 1024 * 1024  # TEMPO_SM100_NOALLOC_SCRATCH_BYTES
 
 _vp, _i, _sz = C.c_void_p, C.c_int, C.c_size_t
 _ip = C.POINTER(C.c_int)
@@ -40,6 +41,7 @@ EXPORTS = {
         _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "tempo_sm100_device_status": (_i, [_ip, _i]),
     "tempo_sm100_version": (C.c_char_p, []),
+    "tempo_sm100_gemm_fp16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
 }
 
 _lock = threading.Lock()

@@ -443,3 +443,59 @@ int tempo_sm100_device_status(int* out4, int reset) {
 const char* tempo_sm100_version(void) { return "tempo-sm100 0.1 (sm_100a, tcgen05/TMA)"; }
 
 }  // extern "C"
+
+// ==========================================================================================
+// Allocation-free entry point: the fp16 GEMM with its split-K scratch in a static device array.
+//
+// Some callers cannot allocate device memory for us: serving frameworks that reserve almost all
+// of HBM up front for their own caching allocator (a foreign cudaMalloc then fails or
+// fragments their pool), latency-critical paths where cudaMalloc/cudaFree would implicitly
+// synchronise the device, and thin FFI callers that have no device allocator to hand us a
+// workspace.  For them the split-K partials and tile counters live in the fixed array below.
+// It is part of the module image, so every GPU that loads this library holds
+// TEMPO_SM100_NOALLOC_SCRATCH_BYTES of it until the process exits.
+// ==========================================================================================
+static __device__ __align__(256) unsigned char tempo_noalloc_scratch[TEMPO_SM100_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::once_flag g_noalloc_once[tempo_sm100::kMaxDevices];
+cudaError_t g_noalloc_err[tempo_sm100::kMaxDevices];
+void* g_noalloc_ptr[tempo_sm100::kMaxDevices];
+}  // namespace
+
+extern "C" int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void* C, int M, int N,
+                                             int K, int lda, int ldb, int ldc, void* stream) {
+  using namespace tempo_sm100;
+  if (!fp16_applicable(A, B, C, M, N, K, lda, ldb, ldc)) return cudaErrorInvalidConfiguration;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  // First call on a device (that device current): resolve the device address of the array.
+  // In host code `tempo_noalloc_scratch` is only a host-side stand-in, never a device pointer.
+  std::call_once(g_noalloc_once[dev], [dev] {
+    void* p = nullptr;
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&p, tempo_noalloc_scratch);
+    g_noalloc_ptr[dev] = g_noalloc_err[dev] == cudaSuccess ? p : nullptr;
+  });
+  if (g_noalloc_err[dev] != cudaSuccess) return g_noalloc_err[dev];
+  void* scratch = g_noalloc_ptr[dev];
+
+  // Same choice as tempo_sm100_gemm_fp16 given a workspace of tempo_sm100_workspace_bytes.
+  Hyper h{};
+  if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, current_sms()))
+    return cudaErrorInvalidConfiguration;
+  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + h.bn - 1) / h.bn);
+  const size_t need = ws_needed(tiles, h.splits, h.bn);
+  if (need > (size_t)TEMPO_SM100_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (need > 0) {
+    // The counters must start at zero; the array keeps whatever the previous call left.
+    e = cudaMemsetAsync(scratch, 0, counters_bytes(tiles), st);
+    if (e != cudaSuccess) return e;
+  }
+  Problem pr{0, A, B, nullptr, nullptr, C, M, N, K, lda, ldb, ldc, 0, scratch,
+             (size_t)TEMPO_SM100_NOALLOC_SCRATCH_BYTES};
+  return run(pr, h, st);
+}

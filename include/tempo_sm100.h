@@ -95,6 +95,29 @@ int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale
  * current device. */
 int tempo_sm100_device_status(int* out4, int reset);
 
+/* Allocation-free variant of tempo_sm100_gemm_fp16 (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory for this library: serving frameworks that
+ * reserve nearly all HBM for their own caching allocator (a foreign cudaMalloc fails or
+ * fragments their pool), latency-critical paths where cudaMalloc/cudaFree would implicitly
+ * synchronise the device, and FFI callers with no device allocator to provide a workspace.
+ * The caller still passes A, B and C; the split-K scratch is a fixed device array of
+ * TEMPO_SM100_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads it until
+ * the process exits.  Never calls cudaMalloc, cudaFree or any allocating routine.
+ *
+ * - The first call on a device resolves the array's device address (cudaGetSymbolAddress, with
+ *   that device current); make that first call before any stream capture on the device.
+ * - Picks the same configuration as tempo_sm100_gemm_fp16 with a full-size workspace; if that
+ *   configuration needs more scratch than TEMPO_SM100_NOALLOC_SCRATCH_BYTES (see
+ *   tempo_sm100_workspace_bytes) the call is rejected with 1 (cudaErrorInvalidValue) and
+ *   launches nothing.
+ * - All calls on a device share the one array and it keeps the last call's contents (the
+ *   counters are cleared on the stream before each launch): calls that may overlap on the GPU
+ *   (different streams, or concurrent host threads) race and must be serialised by the caller. */
+#define TEMPO_SM100_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
+                                  int lda, int ldb, int ldc, void* stream);
+
 /* Library identification string. */
 const char* tempo_sm100_version(void);
 

@@ -32,3 +32,10 @@ def test_version_string_without_gpu():
     from cuda_tempiler_b200 import _lib
     assert b"sm_100a" in _lib.load().tempo_sm100_version()
 
+
+
+def test_noalloc_scratch_size_matches_header():
+    from cuda_tempiler_b200 import _lib
+    text = (ROOT / "include" / "tempo_sm100.h").read_text()
+    m = re.search(r"#define TEMPO_SM100_NOALLOC_SCRATCH_BYTES \((\d+)u \* 1024u \* 1024u\)", text)
+    assert m and int(m.group(1)) * 1024 * 1024 == _lib.NOALLOC_SCRATCH_BYTES
