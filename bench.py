@@ -210,8 +210,8 @@ def run_case(args):
     else:
         G = WL.W8_GROUP_SIZE
         W = torch.randint(0, 256, (N, K), generator=g, device=dev, dtype=torch.uint8)
-        s = (torch.rand(N, K // G, generator=g, device=dev) * 0.019 + 1e-3).half()
-        z = torch.randint(100, 157, (N, K // G), generator=g, device=dev, dtype=torch.uint8)
+        s = (torch.rand(K // G, N, generator=g, device=dev) * 0.019 + 1e-3).half()
+        z = torch.randint(100, 157, (K // G, N), generator=g, device=dev, dtype=torch.uint8)
         f = lambda: ops.gemm_w8a16(A, W, s, z, G)
         by = WL.algorithmic_bytes(M, N, K, 1, "group", G)
     for _ in range(args.warmup):

@@ -12,216 +12,19 @@
 #include <cstring>
 #include <mutex>
 
-#include "gemm_sm100.cuh"
-#include "naive_gemm.cuh"
 #include "tempo_sm100.h"
+#include "launch.cuh"
 
 namespace tempo_sm100 {
-
-
 namespace {
 
-constexpr int kMaxDevices = 64;
-
-// ------------------------------------------------------------------------------------------
-// Driver entry point for cuTensorMapEncodeTiled (no -lcuda link dependency).
-// ------------------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// 2-D row-major tensor [outer][inner] with row stride `ld` elements; box [box_outer][box_inner].
-bool make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, uint64_t inner,
-              uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle sw) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {ld * (uint64_t)esize};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-struct DevInfo {
-  int sms = 0;
-};
-
-DevInfo dev_info(int dev) {
-  static DevInfo info[kMaxDevices];
-  static std::once_flag once[kMaxDevices];
-  if (dev < 0 || dev >= kMaxDevices) return DevInfo{};
-  std::call_once(once[dev], [dev] {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    info[dev].sms = v;
-  });
-  return info[dev];
-}
-
-struct Problem {
-  int wkind;  // 0 fp16, 1 int8 per-channel, 2 uint8 group
-  const void* A;
-  const void* W;
-  const void* scale;
-  const void* zero;
-  void* C;
-  int M, N, K;
-  long long lda, ldw, ldc;
-  int group;
-  void* ws;
-  size_t ws_bytes;
-};
-
-struct Hyper {
-  int bn, swap, splits, group_m, max_ctas;
-};
-
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-size_t counters_bytes(int tiles) { return ((size_t)tiles * sizeof(int) + 255) / 256 * 256; }
-
-size_t ws_needed(int tiles, int splits, int bn) {
-  if (splits <= 1) return 0;
-  return counters_bytes(tiles) + (size_t)tiles * splits * 128 * bn * sizeof(float);
-}
-
-// ------------------------------------------------------------------------------------------
-// Instantiation table.
-// ------------------------------------------------------------------------------------------
-template <int BN, int WQ, bool SWAP>
-cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  using Cfg = SkelCfg<BN, WQ, SWAP>;
-  auto kern = k_gemm_sm100<BN, WQ, SWAP>;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  {
-    // cudaFuncSetAttribute once per instantiation and device (the reference calls it on every
-    // launch, launch.cuh:44-48; it is idempotent but not free).
-    static std::once_flag once[kMaxDevices];
-    static cudaError_t attr_err[kMaxDevices];
-    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    std::call_once(once[dev], [&] {
-      attr_err[dev] =
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    });
-    if (attr_err[dev] != cudaSuccess) return attr_err[dev];
-  }
-  const int rows_p = SWAP ? pr.N : pr.M;
-  const int rows_q = SWAP ? pr.M : pr.N;
-  GemmArgs a{};
-  a.rows_p = rows_p;
-  a.rows_q = rows_q;
-  a.K = pr.K;
-  a.tiles_p = (rows_p + Cfg::BM - 1) / Cfg::BM;
-  a.tiles_q = (rows_q + BN - 1) / BN;
-  a.num_kb = (pr.K + Cfg::BK - 1) / Cfg::BK;
-  a.splits = std::max(1, std::min(h.splits, a.num_kb));
-  const int tiles = a.tiles_p * a.tiles_q;
-  a.num_units = tiles * a.splits;
-  a.group_m = std::max(1, h.group_m);
-  a.C = static_cast<__half*>(pr.C);
-  a.ldc = pr.ldc;
-  if (a.splits > 1) {
-    if (!pr.ws || pr.ws_bytes < ws_needed(tiles, a.splits, BN)) return cudaErrorInvalidValue;
-    a.counters = static_cast<int*>(pr.ws);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + counters_bytes(tiles));
-  }
-  a.scale = static_cast<const __half*>(pr.scale);
-  a.zero = static_cast<const uint8_t*>(pr.zero);
-  a.group_size = pr.group > 0 ? pr.group : 1;
-  a.groups_per_row = pr.group > 0 ? pr.K / pr.group : 1;
-  a.weight_rows = pr.N;
-
-  CUtensorMap mP, mQ, mW, mC;
-  std::memset(&mP, 0, sizeof(mP));
-  std::memset(&mQ, 0, sizeof(mQ));
-  std::memset(&mW, 0, sizeof(mW));
-  std::memset(&mC, 0, sizeof(mC));
-  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  const auto SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
-  bool ok = true;
-  if (SWAP) {
-    if (WQ == 0)
-      ok &= make_map(&mP, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, 128, SW128);
-    else
-      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-    ok &= make_map(&mQ, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, BN, SW128);
-  } else {
-    ok &= make_map(&mP, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, SW128);
-    if (WQ == 0)
-      ok &= make_map(&mQ, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN, SW128);
-    else
-      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
-    ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-  }
-  if (!ok) return cudaErrorInvalidValue;
-
-  const int sms = dev_info(dev).sms;
-  int grid = std::min(a.num_units, h.max_ctas > 0 ? h.max_ctas : sms);
-  if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mP, mQ, mW, mC, a);
-  return cudaGetLastError();
-}
-
-using LaunchFn = cudaError_t (*)(const Problem&, const Hyper&, cudaStream_t);
-
-struct InstEntry {
-  int wkind, bn, swap;
-  LaunchFn fn;
-  const void* kern;
-  int threads, smem, stages, tmem_cols;
-};
-
-#define TEMPO_INST(BN, WQ, SWAP)                                                        \
-  InstEntry {                                                                           \
-    WQ, BN, SWAP, &launch_inst<BN, WQ, SWAP>,                                           \
-        reinterpret_cast<const void*>(&k_gemm_sm100<BN, WQ, SWAP>),                     \
-        SkelCfg<BN, WQ, SWAP>::THREADS, SkelCfg<BN, WQ, SWAP>::SMEM,                    \
-        SkelCfg<BN, WQ, SWAP>::STAGES, SkelCfg<BN, WQ, SWAP>::TMEM_COLS                 \
-  }
-#define TEMPO_INST_WQ(BN, SWAP) TEMPO_INST(BN, 0, SWAP), TEMPO_INST(BN, 1, SWAP), TEMPO_INST(BN, 2, SWAP)
-
-const InstEntry kInst[] = {
-    TEMPO_INST_WQ(16, true),  TEMPO_INST_WQ(32, true),   TEMPO_INST_WQ(64, true),
-    TEMPO_INST_WQ(128, true), TEMPO_INST_WQ(64, false),  TEMPO_INST_WQ(128, false),
-    TEMPO_INST_WQ(256, false),
-};
-
-const InstEntry* find_inst(int wkind, int bn, int swap) {
-  for (const auto& e : kInst)
-    if (e.wkind == wkind && e.bn == bn && e.swap == (swap ? 1 : 0)) return &e;
-  return nullptr;
-}
-
-// ------------------------------------------------------------------------------------------
-// The M-ladder (generated from select.py into dispatch.inc) and the split-K cost model.
-// ------------------------------------------------------------------------------------------
 struct LadderRow {
   int m_max;  // inclusive upper bound on M (0x7fffffff = everything else)
   int bn, swap, group_m;
 };
 
-#include "dispatch.inc"
+#include "gemm_fp16/sm_100a/dispatch.inc"
+#include "gemm_w8a16/sm_100a/dispatch.inc"
 
 const LadderRow* ladder_row(int wkind, int M) {
   const LadderRow* rows = wkind == 0 ? kLadderFp16 : kLadderW8;
@@ -232,22 +35,33 @@ const LadderRow* ladder_row(int wkind, int M) {
   return nullptr;
 }
 
-// Time model in units of one k-block of one tile: waves * (k-blocks per unit + fill), plus a
-// fix-up charge per extra split.  Picks the k-split that best fills `sms` persistent CTAs.
-int choose_splits(int tiles, int num_kb, int sms, int bn, size_t ws_bytes) {
+// Cycle model of one launch, used to pick the k-split (mirrored by the shipped select.py):
+//   SM side:  ceil(units / SMs) waves x (k-blocks per unit x per-k-block + split fix-up).
+//             Per k-block = max(MMA, operand feed): one 128xBNx16 UMMA costs max(BN/2 tensor
+//             cycles, (128+BN)*32 B / 128 B-per-cycle shared-memory reads); the feed is
+//             (128+BN)*128 B per k-block at ~100 B/cycle/SM from L2.  The split fix-up writes
+//             and re-reads a 128xBN fp32 slice (charged 3x for the counter/barrier).
+//   HBM side: compulsory bytes (2MK + w_b NK + 2MN) at ~3400 B/cycle for the whole GPU.
+//   launch:   the larger of the two.
+double launch_cycles(int tiles, int num_kb, int sms, int bn, int s, double hbm_bytes) {
+  const long long units = (long long)tiles * s;
+  const long long waves = (units + sms - 1) / sms;
+  const double mma = 4.0 * std::max(bn / 2.0, (128.0 + bn) / 4.0);
+  const double feed = (128.0 + bn) * 128.0 / 100.0;
+  const double kb = (double)((num_kb + s - 1) / s);
+  const double fixup = s > 1 ? 3.0 * 128.0 * bn * 4.0 / 100.0 + 1500.0 : 0.0;
+  const double sm_side = (double)waves * (kb * std::max(mma, feed) + fixup);
+  return std::max(sm_side, hbm_bytes / 3400.0);
+}
+
+int choose_splits(int tiles, int num_kb, int sms, int bn, size_t ws_bytes, double hbm_bytes) {
   if (sms <= 0) return 1;
-  auto cost = [&](int s) {
-    const long long units = (long long)tiles * s;
-    const long long waves = (units + sms - 1) / sms;
-    const long long per = (num_kb + s - 1) / s;
-    return (double)waves * (double)(per + 4) + (s > 1 ? 2.0 + 0.25 * s : 0.0);
-  };
   int best = 1;
-  double best_c = cost(1);
+  double best_c = launch_cycles(tiles, num_kb, sms, bn, 1, hbm_bytes);
   const int smax = std::min(32, num_kb / 2);
   for (int s = 2; s <= smax; ++s) {
     if (ws_needed(tiles, s, bn) > ws_bytes) break;
-    const double c = cost(s);
+    const double c = launch_cycles(tiles, num_kb, sms, bn, s, hbm_bytes);
     if (c < best_c * 0.97) {
       best = s;
       best_c = c;
@@ -266,35 +80,9 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
   const int tiles = ((rows_p + 127) / 128) * ((rows_q + h.bn - 1) / h.bn);
   const int num_kb = (K + 63) / 64;
-  h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes);
+  const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
+  h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes, hbm);
   return find_inst(wkind, h.bn, h.swap) != nullptr;
-}
-
-bool fp16_applicable(const void* A, const void* B, const void* C, int M, int N, int K, long long lda,
-                     long long ldb, long long ldc) {
-  if (M <= 0 || N <= 0 || K <= 0) return false;
-  if (!A || !B || !C) return false;
-  if ((K % 8) || (N % 8)) return false;
-  if (lda < K || ldb < K || ldc < N) return false;
-  if ((lda % 8) || (ldb % 8) || (ldc % 8)) return false;
-  if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return false;
-  return true;
-}
-
-bool w8_applicable(const void* A, const void* W, const void* scale, const void* zero, const void* C,
-                   int M, int N, int K, long long lda, long long ldw, long long ldc, int kind,
-                   int group) {
-  if (kind != TEMPO_W8_INT8_PER_CHANNEL && kind != TEMPO_W8_UINT8_GROUP) return false;
-  if (M <= 0 || N <= 0 || K <= 0) return false;
-  if (!A || !W || !C || !scale) return false;
-  if ((K % 16) || (N % 8)) return false;
-  if (lda < K || ldw < K || ldc < N) return false;
-  if ((lda % 8) || (ldw % 16) || (ldc % 8)) return false;
-  if (!aligned16(A) || !aligned16(W) || !aligned16(C)) return false;
-  if (kind == TEMPO_W8_UINT8_GROUP) {
-    if (!zero || group <= 0 || (group % 64) || (K % group)) return false;
-  }
-  return true;
 }
 
 cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {

@@ -1,0 +1,259 @@
+// Frozen by the tempolator ship stage for gemm_fp16 / sm_100a.  Do not edit: re-ship.
+// launch.cuh -- host side of the sm_100a GEMM skeleton family: TMA descriptor construction,
+// the instantiation table (one entry per (BN, weight kind, swap) hyperform family member),
+// the persistent-grid launch and the applicability predicates.  Mirrors the reference's
+// shipped launch.cuh (kernels/shipped/gemm_fp16/sm_70/launch.cuh:20-67: POD params,
+// launch_one<...> with the >48 KB dynamic shared-memory opt-in, applicable()).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "kernel.cuh"
+
+#ifndef TEMPO_W8_INT8_PER_CHANNEL
+#define TEMPO_W8_INT8_PER_CHANNEL 1
+#define TEMPO_W8_UINT8_GROUP 2
+#endif
+
+namespace tempo_sm100 {
+namespace {
+constexpr int kMaxDevices = 64;
+
+// ------------------------------------------------------------------------------------------
+// Driver entry point for cuTensorMapEncodeTiled (no -lcuda link dependency).
+// ------------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer][inner] with row stride `ld` elements; box [box_outer][box_inner].
+bool make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, uint64_t inner,
+              uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {ld * (uint64_t)esize};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct DevInfo {
+  int sms = 0;
+};
+
+DevInfo dev_info(int dev) {
+  static DevInfo info[kMaxDevices];
+  static std::once_flag once[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return DevInfo{};
+  std::call_once(once[dev], [dev] {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    info[dev].sms = v;
+  });
+  return info[dev];
+}
+
+struct Problem {
+  int wkind;  // 0 fp16, 1 int8 per-channel, 2 uint8 group
+  const void* A;
+  const void* W;
+  const void* scale;
+  const void* zero;
+  void* C;
+  int M, N, K;
+  long long lda, ldw, ldc;
+  int group;
+  void* ws;
+  size_t ws_bytes;
+};
+
+struct Hyper {
+  int bn, swap, splits, group_m, max_ctas;
+};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+size_t counters_bytes(int tiles) { return ((size_t)tiles * sizeof(int) + 255) / 256 * 256; }
+
+size_t ws_needed(int tiles, int splits, int bn) {
+  if (splits <= 1) return 0;
+  return counters_bytes(tiles) + (size_t)tiles * splits * 128 * bn * sizeof(float);
+}
+
+// ------------------------------------------------------------------------------------------
+// Instantiation table.
+// ------------------------------------------------------------------------------------------
+template <int BN, int WQ, bool SWAP>
+cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  using Cfg = SkelCfg<BN, WQ, SWAP>;
+  auto kern = k_gemm_sm100<BN, WQ, SWAP>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    // cudaFuncSetAttribute once per instantiation and device (the reference calls it on every
+    // launch, launch.cuh:44-48; it is idempotent but not free).
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [&] {
+      attr_err[dev] =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    });
+    if (attr_err[dev] != cudaSuccess) return attr_err[dev];
+  }
+  const int rows_p = SWAP ? pr.N : pr.M;
+  const int rows_q = SWAP ? pr.M : pr.N;
+  GemmArgs a{};
+  a.rows_p = rows_p;
+  a.rows_q = rows_q;
+  a.K = pr.K;
+  a.tiles_p = (rows_p + Cfg::BM - 1) / Cfg::BM;
+  a.tiles_q = (rows_q + BN - 1) / BN;
+  a.num_kb = (pr.K + Cfg::BK - 1) / Cfg::BK;
+  a.splits = std::max(1, std::min(h.splits, a.num_kb));
+  const int tiles = a.tiles_p * a.tiles_q;
+  a.num_units = tiles * a.splits;
+  a.group_m = std::max(1, h.group_m);
+  a.C = static_cast<__half*>(pr.C);
+  a.ldc = pr.ldc;
+  if (a.splits > 1) {
+    if (!pr.ws || pr.ws_bytes < ws_needed(tiles, a.splits, BN)) return cudaErrorInvalidValue;
+    a.counters = static_cast<int*>(pr.ws);
+    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + counters_bytes(tiles));
+  }
+  a.scale = static_cast<const __half*>(pr.scale);
+  a.zero = static_cast<const uint8_t*>(pr.zero);
+  a.group_size = pr.group > 0 ? pr.group : 1;
+  a.groups_per_row = pr.group > 0 ? pr.K / pr.group : 1;
+  a.weight_rows = pr.N;
+
+  CUtensorMap mP, mQ, mW, mC, mS, mZ;
+  std::memset(&mS, 0, sizeof(mS));
+  std::memset(&mZ, 0, sizeof(mZ));
+  std::memset(&mP, 0, sizeof(mP));
+  std::memset(&mQ, 0, sizeof(mQ));
+  std::memset(&mW, 0, sizeof(mW));
+  std::memset(&mC, 0, sizeof(mC));
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const auto SW128 = CU_TENSOR_MAP_SWIZZLE_128B;
+  bool ok = true;
+  if (SWAP) {
+    if (WQ == 0)
+      ok &= make_map(&mP, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, 128, SW128);
+    else
+      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&mQ, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, BN, SW128);
+  } else {
+    ok &= make_map(&mP, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, SW128);
+    if (WQ == 0)
+      ok &= make_map(&mQ, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN, SW128);
+    else
+      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  if (WQ == 2) {
+    // group-wise scale fp16 [K/G][N] and zero uint8 [K/G][N]: one row segment per k-block
+    const int wrows = SWAP ? Cfg::BM : BN;
+    const uint64_t groups = (uint64_t)(pr.K / pr.group);
+    ok &= make_map(&mS, pr.scale, F16, 2, pr.N, groups, pr.N, wrows, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, groups, pr.N, wrows, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+
+  const int sms = dev_info(dev).sms;
+  int grid = std::min(a.num_units, h.max_ctas > 0 ? h.max_ctas : sms);
+  if (grid <= 0) return cudaErrorInvalidConfiguration;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mP, mQ, mW, mC, mS, mZ, a);
+  return cudaGetLastError();
+}
+
+using LaunchFn = cudaError_t (*)(const Problem&, const Hyper&, cudaStream_t);
+
+struct InstEntry {
+  int wkind, bn, swap;
+  LaunchFn fn;
+  const void* kern;
+  int threads, smem, stages, tmem_cols;
+};
+
+#define TEMPO_INST(BN, WQ, SWAP)                                                        \
+  InstEntry {                                                                           \
+    WQ, BN, SWAP, &launch_inst<BN, WQ, SWAP>,                                           \
+        reinterpret_cast<const void*>(&k_gemm_sm100<BN, WQ, SWAP>),                     \
+        SkelCfg<BN, WQ, SWAP>::THREADS, SkelCfg<BN, WQ, SWAP>::SMEM,                    \
+        SkelCfg<BN, WQ, SWAP>::STAGES, SkelCfg<BN, WQ, SWAP>::TMEM_COLS                 \
+  }
+#define TEMPO_INST_WQ(BN, SWAP) TEMPO_INST(BN, 0, SWAP), TEMPO_INST(BN, 1, SWAP), TEMPO_INST(BN, 2, SWAP)
+
+const InstEntry kInst[] = {
+    TEMPO_INST_WQ(16, true),  TEMPO_INST_WQ(32, true),   TEMPO_INST_WQ(64, true),
+    TEMPO_INST_WQ(128, true), TEMPO_INST_WQ(64, false),  TEMPO_INST_WQ(128, false),
+    TEMPO_INST_WQ(256, false),
+};
+
+const InstEntry* find_inst(int wkind, int bn, int swap) {
+  for (const auto& e : kInst)
+    if (e.wkind == wkind && e.bn == bn && e.swap == (swap ? 1 : 0)) return &e;
+  return nullptr;
+}
+
+// ------------------------------------------------------------------------------------------
+// The M-ladder (generated from select.py into dispatch.inc) and the split-K cost model.
+// ------------------------------------------------------------------------------------------
+bool fp16_applicable(const void* A, const void* B, const void* C, int M, int N, int K, long long lda,
+                     long long ldb, long long ldc) {
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (!A || !B || !C) return false;
+  if ((K % 8) || (N % 8)) return false;
+  if (lda < K || ldb < K || ldc < N) return false;
+  if ((lda % 8) || (ldb % 8) || (ldc % 8)) return false;
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return false;
+  return true;
+}
+
+bool w8_applicable(const void* A, const void* W, const void* scale, const void* zero, const void* C,
+                   int M, int N, int K, long long lda, long long ldw, long long ldc, int kind,
+                   int group) {
+  if (kind != TEMPO_W8_INT8_PER_CHANNEL && kind != TEMPO_W8_UINT8_GROUP) return false;
+  if (M <= 0 || N <= 0 || K <= 0) return false;
+  if (!A || !W || !C || !scale) return false;
+  if ((K % 16) || (N % 8)) return false;
+  if (lda < K || ldw < K || ldc < N) return false;
+  if ((lda % 8) || (ldw % 16) || (ldc % 8)) return false;
+  if (!aligned16(A) || !aligned16(W) || !aligned16(C)) return false;
+  if (kind == TEMPO_W8_UINT8_GROUP) {
+    if (!zero || group <= 0 || (group % 64) || (K % group)) return false;
+    if ((N % 16) || !aligned16(scale) || !aligned16(zero)) return false;  // TMA row strides
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace tempo_sm100

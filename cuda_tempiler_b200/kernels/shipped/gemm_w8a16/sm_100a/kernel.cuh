@@ -1,3 +1,274 @@
+// Frozen by the tempolator ship stage for gemm_w8a16 / sm_100a.  Do not edit: re-ship.
+#pragma once
+// ===== sm100_ptx.cuh
+// Thin inline-PTX wrappers for the Blackwell (sm_100a) features the GEMM skeletons use:
+// mbarrier waits with a time limit, TMA tile loads/stores, tcgen05 TMEM allocation, MMA,
+// commit and TMEM->register loads.  Every wrapper is one or two PTX instructions; the
+// instruction and descriptor formats follow the public PTX ISA (tcgen05 chapter) and the
+// CUTLASS sm100 descriptor definitions (cute/arch/mma_sm100_desc.hpp).
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#if defined(__CUDA_ARCH__) && !defined(__CUDA_ARCH_FEAT_SM100_ALL)
+#error "tempo sm100 skeletons must be compiled for sm_100a (tcgen05/TMA path would be compiled out)"
+#endif
+
+namespace tempo_sm100 {
+
+// Device status word written when a bounded wait gives up.  [0] error code (0 = ok,
+// 1 = mbarrier wait timed out), [1] where (role id), [2] blockIdx.x of the first failure.
+// Defined here: the whole library is one translation unit (tempo_sm100.cu).
+__device__ int g_status[4];
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: no legit wait is that long
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false if the CTA-wide abort flag is raised or the time limit passes;
+// on a timeout the first failing block records itself in g_status and raises the abort flag.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                            int where) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      if (atomicCAS(&g_status[0], 0, 1) == 0) {
+        g_status[1] = where;
+        g_status[2] = blockIdx.x;
+      }
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, where);
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tile load global -> shared, completion reported as tx bytes on `bar`.
+// x (innermost coordinate) must be a multiple of 16 bytes / element size.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(cache_hint)
+      : "memory");
+}
+
+// 2-D tile store shared -> global (bulk group).  Out-of-range parts of the box are clipped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// L2 cache-policy hints (createpolicy results) for the TMA loads.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05: TMEM allocation, MMA, commit, TMEM loads
+// ---------------------------------------------------------------------------------------
+// Whole-warp collective.  Writes the allocated TMEM base address into shared memory.
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, fp16 inputs, fp32 accumulate (kind::f16).
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 op previously issued by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// ---------------------------------------------------------------------------------------
+// Descriptors
+// ---------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte
+// swizzle: rows of 64 fp16 (128 B), 8-row swizzle atoms of 1024 B stacked along M/N.
+//   bits  0-13 start address >> 4
+//   bits 16-29 leading byte offset >> 4 (unused for swizzled K-major; 1 by convention)
+//   bits 32-45 stride byte offset >> 4 (distance between 8-row atoms = 1024 B)
+//   bits 46-47 descriptor version (1 on sm_100)
+//   bits 61-63 layout type (2 = 128-byte swizzle)
+__device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16: fp16 A/B, fp32 D, both K-major, shape M x N.
+//   bits 4-5 D format (1 = f32), 7-9 A format (0 = f16), 10-12 B format (0 = f16),
+//   bit 15/16 A/B major (0 = K), bits 17-22 N >> 3, bits 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------------------
+// int8 / uint8 -> fp16 conversion (exact), 4 bytes -> two half2.
+// Published method: place the byte in the mantissa of 1024.0h (0x6400 | byte) with a byte
+// permute, which represents 1024 + byte exactly, then subtract the bias with one half2 op
+// (Kim et al., "Who Says Elephants Can't Run", 2022; also used by FasterTransformer).
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void u8x4_to_h2x2_biased(uint32_t x, __half2& lo, __half2& hi) {
+  // result halves hold 1024 + byte (exact)
+  const uint32_t l = __byte_perm(x, 0x64646464u, 0x5150);
+  const uint32_t h = __byte_perm(x, 0x64646464u, 0x5352);
+  lo = *reinterpret_cast<const __half2*>(&l);
+  hi = *reinterpret_cast<const __half2*>(&h);
+}
+
+}  // namespace tempo_sm100
+
+// ===== kernel.cuh
 // gemm_sm100: the sm_100a GEMM skeleton family (fp16 and W8A16).
 //
 //   D[p, q] = sum_k P[p, k] * Q[q, k]         (both operands K-major, fp32 accumulate)
@@ -22,9 +293,7 @@
 // Persistent: the grid is at most one CTA per SM; CTAs stride over work units
 // (tile_p, tile_q, k-split).  Every mbarrier wait is bounded (2 s) and reports through
 // g_status instead of hanging the GPU.
-#pragma once
 
-#include "sm100_ptx.cuh"
 
 namespace tempo_sm100 {
 
@@ -64,7 +333,11 @@ struct SkelCfg {
   static constexpr int P_OFF = 0;
   static constexpr int Q_OFF = round_up(P_BYTES, 1024);
   static constexpr int RAW_OFF = Q_OFF + round_up(Q_BYTES, 1024);
-  static constexpr int STAGE_BYTES = RAW_OFF + round_up(RAW_BYTES, 1024);
+  // group-wise: this k-block's scale row (fp16) and zero row (uint8) for the tile's weight rows
+  static constexpr int SZ_BYTES = WQ == 2 ? WROWS * 3 : 0;
+  static constexpr int S_OFF = RAW_OFF + RAW_BYTES;
+  static constexpr int Z_OFF = S_OFF + WROWS * 2;
+  static constexpr int STAGE_BYTES = RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024);
   static constexpr int EPI_BYTES = SWAP ? 0 : 4 * 2 * 2048;  // per epilogue warp: 2 x [32][32] fp16
   static constexpr int BAR_BYTES = 512;
   static constexpr int STAGES =
@@ -112,6 +385,7 @@ template <int BN, int WQ, bool SWAP>
 __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapQ,
                  const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapC,
+                 const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapZ,
                  const GemmArgs args) {
   using Cfg = SkelCfg<BN, WQ, SWAP>;
   constexpr int STAGES = Cfg::STAGES;
@@ -142,7 +416,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(deq_bar(s), 4);
+      mbar_init(deq_bar(s), 1);  // one dequant warp owns a stage
       mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -157,6 +431,10 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&mapQ);
     if (WQ) tma_prefetch_desc(&mapW);
+    if (WQ == kWUint8Group) {
+      tma_prefetch_desc(&mapS);
+      tma_prefetch_desc(&mapZ);
+    }
     if (!WQ || !SWAP) tma_prefetch_desc(&mapP);
     if (!SWAP) tma_prefetch_desc(&mapC);
   }
@@ -193,14 +471,21 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             mbar_arrive_expect_tx(full_bar(stage), Cfg::P_BYTES + Cfg::Q_BYTES);
             tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, SWAP ? pol_w : pol_a);
             tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, SWAP ? pol_a : pol_w);
-          } else if (SWAP) {
-            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + Cfg::Q_BYTES);
-            tma_load_2d(smem_u32(raw_ptr(stage)), &mapW, full_bar(stage), kx, tp * Cfg::BM, pol_w);
-            tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, pol_a);
           } else {
-            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + Cfg::P_BYTES);
-            tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, pol_a);
-            tma_load_2d(smem_u32(raw_ptr(stage)), &mapW, full_bar(stage), kx, tq * BN, pol_w);
+            const int wrow0 = SWAP ? tp * Cfg::BM : tq * BN;
+            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + Cfg::SZ_BYTES +
+                                                       (SWAP ? Cfg::Q_BYTES : Cfg::P_BYTES));
+            if (SWAP)
+              tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, pol_a);
+            else
+              tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, pol_a);
+            tma_load_2d(smem_u32(raw_ptr(stage)), &mapW, full_bar(stage), kx, wrow0, pol_w);
+            if (WQ == kWUint8Group) {
+              const int g = kx / args.group_size;
+              const uint32_t sbase = smem_base + stage * Cfg::STAGE_BYTES;
+              tma_load_2d(sbase + Cfg::S_OFF, &mapS, full_bar(stage), wrow0, g, pol_a);
+              tma_load_2d(sbase + Cfg::Z_OFF, &mapZ, full_bar(stage), wrow0, g, pol_a);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -450,64 +735,72 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     if (!SWAP && lane == 0) bulk_wait_group<0>();
   } else {
     // ------------------------------------------------------------------ dequant (W8A16)
+    // Dequant warp d owns every 4th k-block of the CTA's sequence, so four stages are
+    // converted concurrently.  Lane l always handles 16-byte chunk (l & 3) of rows
+    // (l >> 2) + 8 j, so its swizzled destination granules are fixed.
     if (WQ) {
-      const int t = threadIdx.x - 6 * 32;
-      int stage = 0;
-      uint32_t phase = 0;
+      const int dw = warp - 6;
+      const int kc = lane & 3;
+      const int r0 = lane >> 2;
+      const int g0 = ((2 * kc) ^ (r0 & 7)) * 16;
+      const int g1 = ((2 * kc + 1) ^ (r0 & 7)) * 16;
+      constexpr int ROWS_PER_PASS = 8;
+      constexpr int PASSES = Cfg::WROWS / ROWS_PER_PASS;
+      int it = 0;
       for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x) {
         int tile, tp, tq, split, kb0, kb1;
         decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
-        const int wrow0 = SWAP ? tp * Cfg::BM : tq * BN;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if ((it & 3) != dw) continue;
+          const int stage = it % STAGES;
+          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 6)) { ok = false; break; }
-          const uint8_t* raw = raw_ptr(stage);
-          uint8_t* dst = smem + stage * Cfg::STAGE_BYTES + (SWAP ? Cfg::P_OFF : Cfg::Q_OFF);
-          const int g = (kb * Cfg::BK) / (WQ == kWUint8Group ? args.group_size : 1);
-#pragma unroll 2
-          for (int c = t; c < Cfg::WROWS * 4; c += 128) {
-            const int r = c >> 2, kc = c & 3;
-            const uint4 x = *reinterpret_cast<const uint4*>(raw + r * 64 + kc * 16);
-            __half2 h[8];
-            if (WQ == kWInt8PerChannel) {
-              // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
-              const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
-              u8x4_to_h2x2_biased(x.x ^ 0x80808080u, h[0], h[1]);
-              u8x4_to_h2x2_biased(x.y ^ 0x80808080u, h[2], h[3]);
-              u8x4_to_h2x2_biased(x.z ^ 0x80808080u, h[4], h[5]);
-              u8x4_to_h2x2_biased(x.w ^ 0x80808080u, h[6], h[7]);
+          uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
+          const uint8_t* raw = sb + Cfg::RAW_OFF;
+          uint8_t* dst = sb + (SWAP ? Cfg::P_OFF : Cfg::Q_OFF);
+          const __half* srow = reinterpret_cast<const __half*>(sb + Cfg::S_OFF);
+          const uint8_t* zrow = sb + Cfg::Z_OFF;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) h[i] = __hsub2(h[i], bias);
-            } else {
-              const int n = wrow0 + r;
-              __half s = __ushort_as_half(0);
-              uint32_t z = 0;
-              if (n < args.weight_rows && g < args.groups_per_row) {
-                s = __ldg(args.scale + (long long)n * args.groups_per_row + g);
-                z = __ldg(args.zero + (long long)n * args.groups_per_row + g);
+          for (int j0 = 0; j0 < PASSES; j0 += 4) {
+            uint4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              x[u] = *reinterpret_cast<const uint4*>(raw + (r0 + ROWS_PER_PASS * (j0 + u)) * 64 + kc * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int r = r0 + ROWS_PER_PASS * (j0 + u);
+              __half2 h[8];
+              if (WQ == kWInt8PerChannel) {
+                // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
+                const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+                u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[0], h[1]);
+                u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[2], h[3]);
+                u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[4], h[5]);
+                u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[6], h[7]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) h[i] = __hsub2(h[i], bias);
+              } else {
+                // (1024 + q) - (1024 + z) = q - z exactly; one rounding in the scale product.
+                // Rows past N were filled with zeros by TMA, so s = 0 and the weight is 0.
+                const __half2 zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | zrow[r])));
+                const __half2 s2 = __half2half2(srow[r]);
+                u8x4_to_h2x2_biased(x[u].x, h[0], h[1]);
+                u8x4_to_h2x2_biased(x[u].y, h[2], h[3]);
+                u8x4_to_h2x2_biased(x[u].z, h[4], h[5]);
+                u8x4_to_h2x2_biased(x[u].w, h[6], h[7]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
               }
-              // (1024 + q) - (1024 + z) = q - z exactly; one rounding in the scale product
-              const __half2 zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | z)));
-              const __half2 s2 = __half2half2(s);
-              u8x4_to_h2x2_biased(x.x, h[0], h[1]);
-              u8x4_to_h2x2_biased(x.y, h[2], h[3]);
-              u8x4_to_h2x2_biased(x.z, h[4], h[5]);
-              u8x4_to_h2x2_biased(x.w, h[6], h[7]);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
+              const uint4* hv = reinterpret_cast<const uint4*>(h);
+              uint8_t* drow = dst + r * 128;
+              *reinterpret_cast<uint4*>(drow + g0) = hv[0];
+              *reinterpret_cast<uint4*>(drow + g1) = hv[1];
             }
-            const uint4* hv = reinterpret_cast<const uint4*>(h);
-            uint8_t* drow = dst + r * 128;
-            *reinterpret_cast<uint4*>(drow + (((2 * kc) ^ (r & 7)) * 16)) = hv[0];
-            *reinterpret_cast<uint4*>(drow + (((2 * kc + 1) ^ (r & 7)) * 16)) = hv[1];
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(deq_bar(stage));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
         if (!ok) break;
       }
@@ -520,6 +813,73 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+}
+
+}  // namespace tempo_sm100
+
+// The naive INPUT bar: one thread per output element, fp32 accumulation, 16x16 CTAs.  This is
+// the operation of the reference's declared input kernel (kernels/naive/gemm_fp16.cu:60-76,
+// C[m][n] = sum_k A[m][k] * B[n][k]) and its W8A16 analogue (no naive W8A16 input exists in
+// the reference; this one dequantises each weight in fp32 on the fly).
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace tempo_sm100 {
+
+__global__ void k_naive_fp16(const __half* __restrict__ A, const __half* __restrict__ B,
+                             __half* __restrict__ C, int M, int N, int K, long long lda,
+                             long long ldb, long long ldc) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = blockIdx.y * blockDim.y + threadIdx.y;
+  if (m >= M || n >= N) return;
+  const __half* a = A + (long long)m * lda;
+  const __half* b = B + (long long)n * ldb;
+  float acc = 0.f;
+  for (int k = 0; k < K; ++k) acc += __half2float(a[k]) * __half2float(b[k]);
+  C[(long long)m * ldc + n] = __float2half_rn(acc);
+}
+
+__global__ void k_naive_w8a16(const __half* __restrict__ A, const uint8_t* __restrict__ W,
+                              const __half* __restrict__ scale, const uint8_t* __restrict__ zero,
+                              __half* __restrict__ C, int M, int N, int K, long long lda,
+                              long long ldw, long long ldc, int kind, int group) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = blockIdx.y * blockDim.y + threadIdx.y;
+  if (m >= M || n >= N) return;
+  const __half* a = A + (long long)m * lda;
+  const uint8_t* w = W + (long long)n * ldw;
+  float acc = 0.f;
+  if (kind == 1) {
+    for (int k = 0; k < K; ++k) acc += __half2float(a[k]) * (float)(int8_t)w[k];
+    acc *= __half2float(scale[n]);
+  } else {
+    for (int k = 0; k < K; ++k) {
+      const int g = k / group;  // scale and zero are [K/group][N]
+      const float s = __half2float(scale[(long long)g * N + n]);
+      const float z = (float)zero[(long long)g * N + n];
+      acc += __half2float(a[k]) * (((float)w[k] - z) * s);
+    }
+  }
+  C[(long long)m * ldc + n] = __float2half_rn(acc);
+}
+
+inline cudaError_t launch_naive_fp16(const __half* A, const __half* B, __half* C, int M, int N,
+                                     int K, long long lda, long long ldb, long long ldc,
+                                     cudaStream_t st) {
+  const dim3 blk(16, 16), grid((N + 15) / 16, (M + 15) / 16);
+  k_naive_fp16<<<grid, blk, 0, st>>>(A, B, C, M, N, K, lda, ldb, ldc);
+  return cudaGetLastError();
+}
+
+inline cudaError_t launch_naive_w8a16(const __half* A, const uint8_t* W, const __half* scale,
+                                      const uint8_t* zero, __half* C, int M, int N, int K,
+                                      long long lda, long long ldw, long long ldc, int kind,
+                                      int group, cudaStream_t st) {
+  const dim3 blk(16, 16), grid((N + 15) / 16, (M + 15) / 16);
+  k_naive_w8a16<<<grid, blk, 0, st>>>(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, kind, group);
+  return cudaGetLastError();
 }
 
 }  // namespace tempo_sm100

@@ -70,7 +70,7 @@ def gemm_w8a16(A: torch.Tensor, W: torch.Tensor, scale: torch.Tensor,
                zero: torch.Tensor | None = None, group_size: int = 0,
                out: torch.Tensor | None = None, use_workspace: bool = True) -> torch.Tensor:
     """kind: int8 W with scale [N] -> per-channel symmetric; uint8 W with scale/zero
-    [N, K/group_size] -> group-wise asymmetric."""
+    [K/group_size, N] (GPTQ orientation) -> group-wise asymmetric."""
     lib = _lib.load()
     _check_2d(A, "A", torch.float16)
     M, K = A.shape

@@ -1,0 +1,549 @@
+// gemm_sm100: the sm_100a GEMM skeleton family (fp16 and W8A16).
+//
+//   D[p, q] = sum_k P[p, k] * Q[q, k]         (both operands K-major, fp32 accumulate)
+//
+// Non-swapped (prefill):  P = A [M,K] activations, Q = B [N,K] weights, C[p][q] = C[m][n].
+// Swapped (decode, "swap-AB"): P = B [N,K] weights fill the 128-row MMA M side, Q = A [M,K]
+// activations become the narrow MMA N side (BN = 16..128), C[q][p] = C[m][n].
+// This is the op of the reference skeleton (C = A * B^T with B stored [N][K]; reference
+// tempo/plugins/sm70/skeletons/gemm_hmma884/kernel.cuh:587-753 and the shipped
+// kernels/shipped/gemm_fp16/sm_70/launch.cuh:20-26), re-designed for Blackwell:
+//
+//   warp 0        TMA producer: 2-D tiles of P and Q (or the raw 8-bit weight) into a
+//                 STAGES-deep shared-memory ring, completion as mbarrier transaction bytes
+//   warp 1        MMA issuer: allocates TMEM, one thread issues tcgen05.mma (128 x BN x 16)
+//                 into a double-buffered fp32 TMEM accumulator, tcgen05.commit frees stages
+//   warps 2-5     epilogue: tcgen05.ld accumulator -> fp16 -> swizzled staging -> TMA store
+//                 (or direct stores when swapped, or fp32 split-K partials + last-CTA fixup)
+//   warps 6-9     (W8A16 only) dequant: raw int8/uint8 weight tile -> fp16 swizzled tile,
+//                 (q - z) * s for group-wise asymmetric weights; per-channel scale is
+//                 applied in the epilogue.
+//
+// Persistent: the grid is at most one CTA per SM; CTAs stride over work units
+// (tile_p, tile_q, k-split).  Every mbarrier wait is bounded (2 s) and reports through
+// g_status instead of hanging the GPU.
+#pragma once
+
+#include "sm100_ptx.cuh"
+
+namespace tempo_sm100 {
+
+enum WeightQuant : int { kWFp16 = 0, kWInt8PerChannel = 1, kWUint8Group = 2 };
+
+struct GemmArgs {
+  int rows_p, rows_q, K;
+  int tiles_p, tiles_q, num_kb, splits, num_units;
+  int group_m;          // raster group height (in P tiles) for L2 reuse
+  __half* C;
+  long long ldc;        // row stride of C in elements
+  float* ws;            // split-K partials (splits > 1)
+  int* counters;        // per-tile arrival counters (zero between calls)
+  const __half* scale;  // per-channel [N] or group-wise [N][K/group]
+  const uint8_t* zero;  // group-wise [N][K/group]
+  int group_size;       // group-wise quantisation group along K
+  int groups_per_row;   // K / group_size
+  int weight_rows;      // N (rows of the weight operand)
+};
+
+__host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
+__host__ __device__ constexpr int tmem_cols_for(int c) {
+  return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
+}
+
+constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
+
+template <int BN_, int WQ_, bool SWAP_>
+struct SkelCfg {
+  static constexpr int BM = 128, BN = BN_, BK = 64, WQ = WQ_;
+  static constexpr bool SWAP = SWAP_;
+  static constexpr int WROWS = WQ ? (SWAP ? BM : BN) : 0;  // rows of the raw weight tile
+  static constexpr int P_BYTES = BM * BK * 2;
+  static constexpr int Q_BYTES = BN * BK * 2;
+  static constexpr int RAW_BYTES = WROWS * BK;
+  static constexpr int P_OFF = 0;
+  static constexpr int Q_OFF = round_up(P_BYTES, 1024);
+  static constexpr int RAW_OFF = Q_OFF + round_up(Q_BYTES, 1024);
+  // group-wise: this k-block's scale row (fp16) and zero row (uint8) for the tile's weight rows
+  static constexpr int SZ_BYTES = WQ == 2 ? WROWS * 3 : 0;
+  static constexpr int S_OFF = RAW_OFF + RAW_BYTES;
+  static constexpr int Z_OFF = S_OFF + WROWS * 2;
+  static constexpr int STAGE_BYTES = RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024);
+  static constexpr int EPI_BYTES = SWAP ? 0 : 4 * 2 * 2048;  // per epilogue warp: 2 x [32][32] fp16
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int STAGES =
+      cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 12);
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int NUM_WARPS = 6 + (WQ ? 4 : 0);
+  static constexpr int THREADS = NUM_WARPS * 32;
+  static constexpr int TMEM_COLS = tmem_cols_for(2 * BN);
+  static constexpr int CW = BN < 32 ? 16 : 32;  // accumulator columns per tcgen05.ld
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
+  static_assert(SWAP || BN >= 32, "non-swapped epilogue stores 32-column boxes");
+  static_assert(STAGES >= 2, "pipeline needs at least two stages");
+  static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
+};
+
+__device__ __forceinline__ void decode_unit(const GemmArgs& a, int unit, int& tile, int& tp,
+                                            int& tq, int& split, int& kb0, int& kb1) {
+  tile = unit / a.splits;
+  split = unit - tile * a.splits;
+  const int gsz = a.group_m * a.tiles_q;
+  const int g = tile / gsz;
+  const int first = g * a.group_m;
+  const int gm = min(a.tiles_p - first, a.group_m);
+  const int r = tile - g * gsz;
+  tp = first + r % gm;
+  tq = r / gm;
+  kb0 = (int)(((long long)a.num_kb * split) / a.splits);
+  kb1 = (int)(((long long)a.num_kb * (split + 1)) / a.splits);
+}
+
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int BN, int WQ, bool SWAP>
+__global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
+    k_gemm_sm100(const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapQ,
+                 const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapC,
+                 const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapZ,
+                 const GemmArgs args) {
+  using Cfg = SkelCfg<BN, WQ, SWAP>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
+
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto deq_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (3 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (3 * STAGES + 2 + b); };
+  const uint32_t done_bar = bar_base + 8u * (3 * STAGES + 4);
+  auto p_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::P_OFF; };
+  auto q_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::Q_OFF; };
+  auto raw_ptr = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_OFF; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(deq_bar(s), 1);  // one dequant warp owns a stage
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 4);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mapQ);
+    if (WQ) tma_prefetch_desc(&mapW);
+    if (WQ == kWUint8Group) {
+      tma_prefetch_desc(&mapS);
+      tma_prefetch_desc(&mapZ);
+    }
+    if (!WQ || !SWAP) tma_prefetch_desc(&mapP);
+    if (!SWAP) tma_prefetch_desc(&mapC);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      // Weights streamed exactly once (swapped decode) go evict-first; the small activation
+      // operand is re-read by every CTA and stays.  Prefill re-reads both: normal policy.
+      const uint64_t pol_w = SWAP ? policy_evict_first() : policy_evict_normal();
+      const uint64_t pol_a = SWAP ? policy_evict_last() : policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, 1)) {
+            ok = false;
+            break;
+          }
+          const int kx = kb * Cfg::BK;
+          if (WQ == kWFp16) {
+            mbar_arrive_expect_tx(full_bar(stage), Cfg::P_BYTES + Cfg::Q_BYTES);
+            tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, SWAP ? pol_w : pol_a);
+            tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, SWAP ? pol_a : pol_w);
+          } else {
+            const int wrow0 = SWAP ? tp * Cfg::BM : tq * BN;
+            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + Cfg::SZ_BYTES +
+                                                       (SWAP ? Cfg::Q_BYTES : Cfg::P_BYTES));
+            if (SWAP)
+              tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, pol_a);
+            else
+              tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, pol_a);
+            tma_load_2d(smem_u32(raw_ptr(stage)), &mapW, full_bar(stage), kx, wrow0, pol_w);
+            if (WQ == kWUint8Group) {
+              const int g = kx / args.group_size;
+              const uint32_t sbase = smem_base + stage * Cfg::STAGE_BYTES;
+              tma_load_2d(sbase + Cfg::S_OFF, &mapS, full_bar(stage), wrow0, g, pol_a);
+              tma_load_2d(sbase + Cfg::Z_OFF, &mapZ, full_bar(stage), wrow0, g, pol_a);
+            }
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain: every load this thread issued must have landed before the CTA can exit
+      // (normally already true; matters only after an abort).
+      const int pending = issued < STAGES ? issued : STAGES;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < pending; ++i) {
+        if (--s < 0) {
+          s = STAGES - 1;
+          ph ^= 1u;
+        }
+        mbar_drain(full_bar(s), ph, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(Cfg::BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int lu = 0;
+      for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x, ++lu) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        const int buf = lu & 1;
+        const uint32_t uphase = (lu >> 1) & 1;
+        if (!mbar_wait(tempty_bar(buf), uphase ^ 1u, abort_flag, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 3)) { ok = false; break; }
+          if (WQ && !mbar_wait(deq_bar(stage), phase, abort_flag, 4)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t pa = p_addr(stage), qa = q_addr(stage);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            umma_f16_ss(d_tmem, sdesc_k_sw128(pa + k * 32), sdesc_k_sw128(qa + k * 32), idesc,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(buf));
+      }
+      // Wait for every MMA this thread issued before TMEM is released.
+      umma_commit(done_bar);
+      mbar_drain(done_bar, 0, 100000000ull);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+    uint8_t* stage_buf = epi_smem + (warp - 2) * 4096;
+    int sb = 0;
+    int lu = 0;
+    for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x, ++lu) {
+      int tile, tp, tq, split, kb0, kb1;
+      decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+      const int buf = lu & 1;
+      const uint32_t uphase = (lu >> 1) & 1;
+      if (!mbar_wait(tfull_bar(buf), uphase, abort_flag, 5)) break;
+      tc_fence_after();
+      const uint32_t t_acc = t_lane + buf * BN;
+      const int p = tp * Cfg::BM + row;
+      const int q0 = tq * BN;
+
+      if (args.splits == 1 && !SWAP) {
+        // fp16 tile through swizzled staging and TMA stores, 32 columns per box.
+        // chunks that hold at least one in-range column; boxes wholly below M are skipped
+        const int live_cols = args.rows_q - q0;
+        const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
+        const bool rows_live = tp * Cfg::BM + quad * 32 < args.rows_p;
+#pragma unroll 1
+        for (int c = 0; c < nchunk; ++c) {
+          uint32_t v[32];
+          tmem_ld_x32(t_acc + c * 32, v);
+          tmem_wait_ld();
+          if (c == nchunk - 1) {
+            // accumulator fully read: hand the TMEM buffer back to the MMA warp early
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(buf));
+          }
+          if (!rows_live) continue;
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          if (WQ == kWInt8PerChannel) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int q = q0 + c * 32 + j;
+              f[j] *= __half2float(q < args.weight_rows ? __ldg(args.scale + q) : __half(0.f));
+            }
+          }
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          uint8_t* sbuf = stage_buf + sb * 2048;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 w;
+            w.x = pack_half2(f[8 * g + 0], f[8 * g + 1]);
+            w.y = pack_half2(f[8 * g + 2], f[8 * g + 3]);
+            w.z = pack_half2(f[8 * g + 4], f[8 * g + 5]);
+            w.w = pack_half2(f[8 * g + 6], f[8 * g + 7]);
+            const int pg = g ^ ((lane >> 1) & 3);  // 64-byte swizzle
+            *reinterpret_cast<uint4*>(sbuf + lane * 64 + pg * 16) = w;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&mapC, smem_u32(sbuf), q0 + c * 32, tp * Cfg::BM + quad * 32);
+            bulk_commit_group();
+          }
+          sb ^= 1;
+        }
+      } else if (args.splits == 1) {
+        // swapped: C[q][p]; lanes run along p (= n), so each column store is coalesced.
+        const float sc =
+            (WQ == kWInt8PerChannel && p < args.rows_p) ? __half2float(__ldg(args.scale + p)) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < BN / Cfg::CW; ++c) {
+          uint32_t v[32];
+          if (Cfg::CW == 32) {
+            tmem_ld_x32(t_acc + c * 32, v);
+          } else {
+            uint32_t (&v16)[16] = *reinterpret_cast<uint32_t(*)[16]>(v);
+            tmem_ld_x16(t_acc + c * 16, v16);
+          }
+          tmem_wait_ld();
+          if (c == BN / Cfg::CW - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(buf));
+          }
+          if (p < args.rows_p) {
+#pragma unroll
+            for (int j = 0; j < Cfg::CW; ++j) {
+              const int q = q0 + c * Cfg::CW + j;
+              if (q < args.rows_q)
+                args.C[(long long)q * args.ldc + p] = __float2half_rn(__uint_as_float(v[j]) * sc);
+            }
+          }
+        }
+      } else {
+        // split-K: fp32 partial slice, [column][row] so the warp's stores are coalesced.
+        float* part = args.ws + ((long long)tile * args.splits + split) * (Cfg::BM * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN / Cfg::CW; ++c) {
+          uint32_t v[32];
+          if (Cfg::CW == 32) {
+            tmem_ld_x32(t_acc + c * 32, v);
+          } else {
+            uint32_t (&v16)[16] = *reinterpret_cast<uint32_t(*)[16]>(v);
+            tmem_ld_x16(t_acc + c * 16, v16);
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < Cfg::CW; ++j)
+            __stcg(part + (c * Cfg::CW + j) * Cfg::BM + row, __uint_as_float(v[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar(buf));
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(args.counters + tile, 1);
+          const int last = (old == args.splits - 1);
+          if (last) atomicExch(args.counters + tile, 0);  // ready for the next call
+          *last_flag = last;
+        }
+        named_barrier_sync(1, 128);
+        if (*last_flag) {
+          __threadfence();
+          // Sum the k-slices in split order (deterministic), 32 columns at a time with all 32
+          // loads of a slice independent, so each slice costs one L2 round trip per chunk.
+          const float* base = args.ws + (long long)tile * args.splits * (Cfg::BM * BN);
+          const float sc_row = (SWAP && WQ == kWInt8PerChannel && p < args.rows_p)
+                                   ? __half2float(__ldg(args.scale + p)) : 1.f;
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += Cfg::CW) {
+            if (q0 + c0 >= args.rows_q || p >= args.rows_p) break;
+            float acc[Cfg::CW];
+#pragma unroll
+            for (int i = 0; i < Cfg::CW; ++i) acc[i] = 0.f;
+            const float* col = base + c0 * Cfg::BM + row;
+            int s = 0;
+#pragma unroll 1
+            for (; s + 2 <= args.splits; s += 2) {
+              float x[Cfg::CW], y[Cfg::CW];
+#pragma unroll
+              for (int i = 0; i < Cfg::CW; ++i) {
+                x[i] = __ldcg(col + (long long)s * (Cfg::BM * BN) + i * Cfg::BM);
+                y[i] = __ldcg(col + (long long)(s + 1) * (Cfg::BM * BN) + i * Cfg::BM);
+              }
+#pragma unroll
+              for (int i = 0; i < Cfg::CW; ++i) acc[i] = (acc[i] + x[i]) + y[i];
+            }
+            if (s < args.splits) {
+#pragma unroll
+              for (int i = 0; i < Cfg::CW; ++i)
+                acc[i] += __ldcg(col + (long long)s * (Cfg::BM * BN) + i * Cfg::BM);
+            }
+            if (SWAP) {
+#pragma unroll
+              for (int i = 0; i < Cfg::CW; ++i) {
+                const int q = q0 + c0 + i;
+                if (q < args.rows_q)
+                  args.C[(long long)q * args.ldc + p] = __float2half_rn(acc[i] * sc_row);
+              }
+            } else {
+#pragma unroll
+              for (int i0 = 0; i0 < Cfg::CW; i0 += 8) {
+                const int q = q0 + c0 + i0;
+                if (q >= args.rows_q) break;
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  o[i] = acc[i0 + i] *
+                         (WQ == kWInt8PerChannel ? __half2float(__ldg(args.scale + q + i)) : 1.f);
+                uint4 w;
+                w.x = pack_half2(o[0], o[1]);
+                w.y = pack_half2(o[2], o[3]);
+                w.z = pack_half2(o[4], o[5]);
+                w.w = pack_half2(o[6], o[7]);
+                *reinterpret_cast<uint4*>(args.C + (long long)p * args.ldc + q) = w;
+              }
+            }
+          }
+        }
+      }
+    }
+    if (!SWAP && lane == 0) bulk_wait_group<0>();
+  } else {
+    // ------------------------------------------------------------------ dequant (W8A16)
+    // Dequant warp d owns every 4th k-block of the CTA's sequence, so four stages are
+    // converted concurrently.  Lane l always handles 16-byte chunk (l & 3) of rows
+    // (l >> 2) + 8 j, so its swizzled destination granules are fixed.
+    if (WQ) {
+      const int dw = warp - 6;
+      const int kc = lane & 3;
+      const int r0 = lane >> 2;
+      const int g0 = ((2 * kc) ^ (r0 & 7)) * 16;
+      const int g1 = ((2 * kc + 1) ^ (r0 & 7)) * 16;
+      constexpr int ROWS_PER_PASS = 8;
+      constexpr int PASSES = Cfg::WROWS / ROWS_PER_PASS;
+      int it = 0;
+      for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if ((it & 3) != dw) continue;
+          const int stage = it % STAGES;
+          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 6)) { ok = false; break; }
+          uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
+          const uint8_t* raw = sb + Cfg::RAW_OFF;
+          uint8_t* dst = sb + (SWAP ? Cfg::P_OFF : Cfg::Q_OFF);
+          const __half* srow = reinterpret_cast<const __half*>(sb + Cfg::S_OFF);
+          const uint8_t* zrow = sb + Cfg::Z_OFF;
+#pragma unroll
+          for (int j0 = 0; j0 < PASSES; j0 += 4) {
+            uint4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              x[u] = *reinterpret_cast<const uint4*>(raw + (r0 + ROWS_PER_PASS * (j0 + u)) * 64 + kc * 16);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int r = r0 + ROWS_PER_PASS * (j0 + u);
+              __half2 h[8];
+              if (WQ == kWInt8PerChannel) {
+                // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
+                const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+                u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[0], h[1]);
+                u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[2], h[3]);
+                u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[4], h[5]);
+                u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[6], h[7]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) h[i] = __hsub2(h[i], bias);
+              } else {
+                // (1024 + q) - (1024 + z) = q - z exactly; one rounding in the scale product.
+                // Rows past N were filled with zeros by TMA, so s = 0 and the weight is 0.
+                const __half2 zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | zrow[r])));
+                const __half2 s2 = __half2half2(srow[r]);
+                u8x4_to_h2x2_biased(x[u].x, h[0], h[1]);
+                u8x4_to_h2x2_biased(x[u].y, h[2], h[3]);
+                u8x4_to_h2x2_biased(x[u].z, h[4], h[5]);
+                u8x4_to_h2x2_biased(x[u].w, h[6], h[7]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
+              }
+              const uint4* hv = reinterpret_cast<const uint4*>(h);
+              uint8_t* drow = dst + r * 128;
+              *reinterpret_cast<uint4*>(drow + g0) = hv[0];
+              *reinterpret_cast<uint4*>(drow + g1) = hv[1];
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(deq_bar(stage));
+        }
+        if (!ok) break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace tempo_sm100

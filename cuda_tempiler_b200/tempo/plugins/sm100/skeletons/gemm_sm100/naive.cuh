@@ -37,11 +37,10 @@ __global__ void k_naive_w8a16(const __half* __restrict__ A, const uint8_t* __res
     for (int k = 0; k < K; ++k) acc += __half2float(a[k]) * (float)(int8_t)w[k];
     acc *= __half2float(scale[n]);
   } else {
-    const int G = K / group;
     for (int k = 0; k < K; ++k) {
-      const int g = k / group;
-      const float s = __half2float(scale[(long long)n * G + g]);
-      const float z = (float)zero[(long long)n * G + g];
+      const int g = k / group;  // scale and zero are [K/group][N]
+      const float s = __half2float(scale[(long long)g * N + n]);
+      const float z = (float)zero[(long long)g * N + n];
       acc += __half2float(a[k]) * (((float)w[k] - z) * s);
     }
   }

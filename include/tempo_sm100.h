@@ -35,8 +35,8 @@ extern "C" {
 
 /* Weight quantisation kinds for the W8A16 op. */
 #define TEMPO_W8_INT8_PER_CHANNEL 1  /* int8 W [N][K], fp16 scale [N]; W = q * s[n]           */
-#define TEMPO_W8_UINT8_GROUP 2       /* uint8 W [N][K], fp16 scale/uint8 zero [N][K/g];
-                                        W = (q - z[n][k/g]) * s[n][k/g]                     */
+#define TEMPO_W8_UINT8_GROUP 2       /* uint8 W [N][K], fp16 scale/uint8 zero [K/g][N] (GPTQ's
+                                        scales and byte view of qzeros); W = (q - z) * s      */
 
 /* Replaces tempo::gen::applicable(const GemmParams&) (launch.cuh:59-67).  1 = covered. */
 int tempo_sm100_gemm_fp16_applicable(const void* A, const void* B, const void* C, int M, int N,
@@ -51,8 +51,9 @@ int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, i
  * tempo/plugins/sm70/skeletons/gemm_w8a16/kernel.cuh:226-296, its GPTQ reconstruction formula
  * bench/gemm_baseline.py:214-231).  W is [N][K] 8-bit, row stride ldw (bytes, multiple of 16).
  * quant_kind TEMPO_W8_INT8_PER_CHANNEL: scale [N], zero ignored, group_size ignored.
- * quant_kind TEMPO_W8_UINT8_GROUP: scale fp16 [N][K/group_size], zero uint8 [N][K/group_size],
- * group_size a multiple of 64 dividing K. */
+ * quant_kind TEMPO_W8_UINT8_GROUP: scale fp16 [K/group_size][N], zero uint8 [K/group_size][N]
+ * (GPTQ's scales array and the byte view of its qzeros, zero-copy), group_size a multiple of 64
+ * dividing K, N a multiple of 16, scale and zero 16-byte aligned. */
 int tempo_sm100_gemm_w8a16_applicable(const void* A, const void* W, const void* scale,
                                       const void* zero, const void* C, int M, int N, int K,
                                       int lda, int ldw, int ldc, int quant_kind, int group_size);

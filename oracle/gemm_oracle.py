@@ -50,10 +50,11 @@ def dequant_per_channel(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
 
 
 def dequant_group(q: np.ndarray, scale: np.ndarray, zero: np.ndarray, group: int) -> np.ndarray:
-    """uint8 q [N,K], fp16 scale [N,K/G], uint8 zero [N,K/G] -> fp32 (q - z[g]) * s[g]."""
+    """uint8 q [N,K], fp16 scale [K/G,N], uint8 zero [K/G,N] (GPTQ orientation) -> fp32
+    (q[n,k] - z[k//G,n]) * s[k//G,n]."""
     N, K = q.shape
-    s = np.repeat(scale.astype(np.float32), group, axis=1)[:, :K]
-    z = np.repeat(zero.astype(np.float32), group, axis=1)[:, :K]
+    s = np.repeat(scale.astype(np.float32), group, axis=0)[:K].T
+    z = np.repeat(zero.astype(np.float32), group, axis=0)[:K].T
     return (q.astype(np.float32) - z) * s
 
 
@@ -103,12 +104,13 @@ def inputs_w8_per_channel(M: int, N: int, K: int, seed: int = 2):
 
 
 def inputs_w8_group(M: int, N: int, K: int, group: int = 128, seed: int = 3):
-    """Config 4: uint8 q U[0,255] [N,K], fp16 scale U(1e-3,2e-2) [N,K/G], uint8 zero U[100,156]."""
+    """Config 4: uint8 q U[0,255] [N,K], fp16 scale U(1e-3,2e-2) [K/G,N], uint8 zero U[100,156]
+    [K/G,N] (GPTQ orientation)."""
     rng = np.random.default_rng(seed)
     a = rng.standard_normal((M, K), dtype=np.float32).astype(np.float16)
     q = rng.integers(0, 256, (N, K), dtype=np.int16).astype(np.uint8)
-    scale = rng.uniform(1e-3, 2e-2, (N, K // group)).astype(np.float16)
-    zero = rng.integers(100, 157, (N, K // group), dtype=np.int16).astype(np.uint8)
+    scale = rng.uniform(1e-3, 2e-2, (K // group, N)).astype(np.float16)
+    zero = rng.integers(100, 157, (K // group, N), dtype=np.int16).astype(np.uint8)
     return a, q, scale, zero
 
 

@@ -73,3 +73,33 @@ def test_naive_w8(dev):
     assert r <= TOL
     r = _grp(40, 136, 256, lambda A, W, s, z, G, C: C.copy_(ops.naive_gemm_w8a16(A, W, s, z, G)))
     assert r <= TOL
+
+
+def test_resources_match_python_plan(dev):
+    """The plugin's Python shared-memory plan equals what the library launches with."""
+    import ctypes as C
+    from cuda_tempiler_b200 import _lib
+    from cuda_tempiler_b200.tempo.plugins.sm100.skeletons_py import skel_cfg
+    lib = _lib.load()
+    for wq in (0, 1, 2):
+        for bn, swap in HYPER:
+            out = (C.c_int * 6)()
+            assert lib.tempo_sm100_hyperform_resources(wq, bn, int(swap), out) == 0
+            c = skel_cfg(bn, wq, swap)
+            assert (out[0], out[1], out[2], out[3]) == (c["threads"], c["smem"], c["stages"], c["tmem_cols"])
+            assert out[5] == 0, "local memory (spills/stack) in an instantiation"
+
+
+def test_gptq_checkpoint_layout_end_to_end(dev):
+    """GPTQ arrays (reference generator output, golden fixture) -> repack -> kernel."""
+    import os
+    from cuda_tempiler_b200 import ops
+    from cuda_tempiler_b200.gptq import dequantize, repack_gptq_int8
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "gptq_int8.npz"))
+    W, s, z = repack_gptq_int8(torch.from_numpy(d["qweight"]), torch.from_numpy(d["qzeros"]),
+                               torch.from_numpy(d["scales"]), 128)
+    a = np.random.default_rng(9).standard_normal((24, 256)).astype(np.float16)
+    C = ops.gemm_w8a16(torch.from_numpy(a).cuda(), W.cuda(), s.cuda(), z.cuda(), 128)
+    torch.cuda.synchronize()
+    ref = a.astype(np.float32) @ d["W"].astype(np.float32)
+    assert O.rel_l2(C.cpu().numpy(), ref) <= TOL
