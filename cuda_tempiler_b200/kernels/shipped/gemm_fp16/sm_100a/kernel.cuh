@@ -194,6 +194,36 @@ __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: A (128 rows x 16 k) read from TMEM, one
+// row per lane, two consecutive k values (fp16) per 32-bit column.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread, register -> TMEM.
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op previously issued by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile(
@@ -326,8 +356,11 @@ template <int BN_, int WQ_, bool SWAP_>
 struct SkelCfg {
   static constexpr int BM = 128, BN = BN_, BK = 64, WQ = WQ_;
   static constexpr bool SWAP = SWAP_;
+  // Swapped 8-bit weights are dequantised straight into TMEM as the MMA's A operand
+  // (tcgen05.mma A-from-TMEM); no fp16 copy of the weight tile ever lands in shared memory.
+  static constexpr bool TA = WQ != 0 && SWAP;
   static constexpr int WROWS = WQ ? (SWAP ? BM : BN) : 0;  // rows of the raw weight tile
-  static constexpr int P_BYTES = BM * BK * 2;
+  static constexpr int P_BYTES = TA ? 0 : BM * BK * 2;
   static constexpr int Q_BYTES = BN * BK * 2;
   static constexpr int RAW_BYTES = WROWS * BK;
   static constexpr int P_OFF = 0;
@@ -340,16 +373,20 @@ struct SkelCfg {
   static constexpr int STAGE_BYTES = RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024);
   static constexpr int EPI_BYTES = SWAP ? 0 : 4 * 2 * 2048;  // per epilogue warp: 2 x [32][32] fp16
   static constexpr int BAR_BYTES = 512;
+  // TMEM: 2 x BN accumulator columns, plus (TA) 32 columns of fp16 A per stage
   static constexpr int STAGES =
-      cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 12);
+      cmin(cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 12),
+           TA ? (512 - 2 * BN) / 32 : 12);
+  static constexpr int A_TMEM_COL = 2 * BN;  // first TMEM column of the A stages (TA)
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-  static constexpr int NUM_WARPS = 6 + (WQ ? 4 : 0);
+  static constexpr int NUM_WARPS = 6 + (TA ? 8 : (WQ ? 4 : 0));
   static constexpr int THREADS = NUM_WARPS * 32;
-  static constexpr int TMEM_COLS = tmem_cols_for(2 * BN);
+  static constexpr int TMEM_COLS = TA ? 512 : tmem_cols_for(2 * BN);
   static constexpr int CW = BN < 32 ? 16 : 32;  // accumulator columns per tcgen05.ld
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
   static_assert(SWAP || BN >= 32, "non-swapped epilogue stores 32-column boxes");
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
+  static_assert(!TA || BN <= 128, "TMEM holds 2 x BN accumulator columns plus the A stages");
   static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
 };
 
@@ -416,7 +453,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(deq_bar(s), 1);  // one dequant warp owns a stage
+      mbar_init(deq_bar(s), Cfg::TA ? 4 : 1);  // TA: 4 quadrant warps; else 1 warp per stage
       mbar_init(empty_bar(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -529,10 +566,18 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
           if (WQ && !mbar_wait(deq_bar(stage), phase, abort_flag, 4)) { ok = false; break; }
           tc_fence_after();
           const uint32_t pa = p_addr(stage), qa = q_addr(stage);
+          if (Cfg::TA) {
+            const uint32_t a_tmem = tmem_base + Cfg::A_TMEM_COL + stage * 32;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 16; ++k) {
-            umma_f16_ss(d_tmem, sdesc_k_sw128(pa + k * 32), sdesc_k_sw128(qa + k * 32), idesc,
-                        (kb > kb0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < Cfg::BK / 16; ++k)
+              umma_f16_ts(d_tmem, a_tmem + k * 8, sdesc_k_sw128(qa + k * 32), idesc,
+                          (kb > kb0 || k > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int k = 0; k < Cfg::BK / 16; ++k) {
+              umma_f16_ss(d_tmem, sdesc_k_sw128(pa + k * 32), sdesc_k_sw128(qa + k * 32), idesc,
+                          (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           umma_commit(empty_bar(stage));
           if (++stage == STAGES) {
@@ -735,10 +780,69 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     if (!SWAP && lane == 0) bulk_wait_group<0>();
   } else {
     // ------------------------------------------------------------------ dequant (W8A16)
-    // Dequant warp d owns every 4th k-block of the CTA's sequence, so four stages are
-    // converted concurrently.  Lane l always handles 16-byte chunk (l & 3) of rows
+    // Dequant warp d owns the stages s with s % 4 == d, so up to four stages are converted
+    // concurrently.  Lane l always handles 16-byte chunk (l & 3) of rows
     // (l >> 2) + 8 j, so its swizzled destination granules are fixed.
-    if (WQ) {
+    if (Cfg::TA) {
+      // Two groups of four warps alternate stages; within a group warp (w & 3) converts the
+      // 32 weight rows of its TMEM lane quadrant, one row per thread: 64 raw bytes (64-byte
+      // swizzled by TMA) -> 32 packed fp16 pairs -> tcgen05.st into the stage's A columns.
+      const int grp = (warp - 6) >> 2;
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::A_TMEM_COL;
+      int it = 0;
+      for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          // a stage always has the same owner, so no owner ever skips one of its phases
+          const int stage = it % STAGES;
+          if ((stage & 1) != grp) continue;
+          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 6)) { ok = false; break; }
+          const uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
+          const uint8_t* raw = sb + Cfg::RAW_OFF + r * 64;
+          const int sw = (r >> 1) & 3;  // 64-byte swizzle: granule j lives at j ^ sw
+          uint4 x[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) x[j] = *reinterpret_cast<const uint4*>(raw + ((j ^ sw) * 16));
+          __half2 h[32];
+          if (WQ == kWInt8PerChannel) {
+            const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              u8x4_to_h2x2_biased(x[j].x ^ 0x80808080u, h[8 * j + 0], h[8 * j + 1]);
+              u8x4_to_h2x2_biased(x[j].y ^ 0x80808080u, h[8 * j + 2], h[8 * j + 3]);
+              u8x4_to_h2x2_biased(x[j].z ^ 0x80808080u, h[8 * j + 4], h[8 * j + 5]);
+              u8x4_to_h2x2_biased(x[j].w ^ 0x80808080u, h[8 * j + 6], h[8 * j + 7]);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) h[i] = __hsub2(h[i], bias);
+          } else {
+            const __half2 zb = __half2half2(__ushort_as_half(
+                (unsigned short)(0x6400u | sb[Cfg::Z_OFF + r])));
+            const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[r]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              u8x4_to_h2x2_biased(x[j].x, h[8 * j + 0], h[8 * j + 1]);
+              u8x4_to_h2x2_biased(x[j].y, h[8 * j + 2], h[8 * j + 3]);
+              u8x4_to_h2x2_biased(x[j].z, h[8 * j + 4], h[8 * j + 5]);
+              u8x4_to_h2x2_biased(x[j].w, h[8 * j + 6], h[8 * j + 7]);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
+          }
+          tmem_st_x32(t_row + stage * 32, *reinterpret_cast<const uint32_t(*)[32]>(h));
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(deq_bar(stage));
+        }
+        if (!ok) break;
+      }
+    } else if (WQ) {
       const int dw = warp - 6;
       const int kc = lane & 3;
       const int r0 = lane >> 2;
@@ -752,8 +856,9 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
         decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          if ((it & 3) != dw) continue;
+          // a stage always has the same owner, so no owner ever skips one of its phases
           const int stage = it % STAGES;
+          if ((stage & 3) != dw) continue;
           const uint32_t phase = (uint32_t)((it / STAGES) & 1);
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 6)) { ok = false; break; }
           uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;

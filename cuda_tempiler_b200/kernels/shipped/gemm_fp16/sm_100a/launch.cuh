@@ -168,7 +168,9 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
     if (WQ == 0)
       ok &= make_map(&mP, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, 128, SW128);
     else
-      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+      // one 64-byte weight row per dequant thread: the 64-byte swizzle keeps its reads
+      // bank-conflict free
+      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B);
     ok &= make_map(&mQ, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, BN, SW128);
   } else {
     ok &= make_map(&mP, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, SW128);

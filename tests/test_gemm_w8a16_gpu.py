@@ -34,7 +34,8 @@ def _grp(M, N, K, fn, G=128, seed=3):
     return O.rel_l2(c, ref)
 
 
-SHAPES = [(1, 136, 256), (5, 520, 1024), (16, 1024, 512), (64, 264, 384), (200, 776, 1024),
+# N % 16 == 0: group-wise scale/zero rows are fetched by TMA (16-byte row strides)
+SHAPES = [(1, 144, 256), (5, 528, 1024), (16, 1024, 512), (64, 272, 384), (200, 784, 1024),
           (512, 1040, 2048)]
 
 
@@ -60,18 +61,18 @@ HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, Fal
 def test_every_hyperform(dev, bn, swap, splits):
     from cuda_tempiler_b200 import ops
     M = 24 if swap else 260
-    r1 = _pc(M, 776, 1024, lambda A, W, s, C: ops.gemm_hyperform(
+    r1 = _pc(M, 784, 1024, lambda A, W, s, C: ops.gemm_hyperform(
         A, W, bn=bn, swap=swap, splits=splits, scale=s, out=C))
-    r2 = _grp(M, 776, 1024, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+    r2 = _grp(M, 784, 1024, lambda A, W, s, z, G, C: ops.gemm_hyperform(
         A, W, bn=bn, swap=swap, splits=splits, scale=s, zero=z, group_size=G, out=C))
     assert r1 <= TOL and r2 <= TOL, (r1, r2)
 
 
 def test_naive_w8(dev):
     from cuda_tempiler_b200 import ops
-    r = _pc(40, 136, 256, lambda A, W, s, C: C.copy_(ops.naive_gemm_w8a16(A, W, s)))
+    r = _pc(40, 144, 256, lambda A, W, s, C: C.copy_(ops.naive_gemm_w8a16(A, W, s)))
     assert r <= TOL
-    r = _grp(40, 136, 256, lambda A, W, s, z, G, C: C.copy_(ops.naive_gemm_w8a16(A, W, s, z, G)))
+    r = _grp(40, 144, 256, lambda A, W, s, z, G, C: C.copy_(ops.naive_gemm_w8a16(A, W, s, z, G)))
     assert r <= TOL
 
 

@@ -29,10 +29,11 @@ def _noalloc(lib, A, B, out):
 def test_noalloc_matches_workspace_entry_two_calls(dev):
     from cuda_tempiler_b200 import _lib, ops
     lib = _lib.load()
-    # two different problems back to back; both use split-K, so both go through the scratch
-    cases = [(16, 3840, 4096), (8, 8192, 3840)]
-    for M, N, K in cases:
-        assert ops.select(0, M, N, K)["splits"] > 1
+    # two different problems back to back that both use split-K, so both go through the scratch
+    cands = [(16, 3840, 15360), (8, 3840, 15360), (16, 3840, 4096), (8, 8192, 3840),
+             (1, 5120, 17408), (32, 5120, 8192)]
+    cases = [c for c in cands if ops.select(0, *c)["splits"] > 1][:2]
+    assert len(cases) == 2, "no candidate problem takes the split-K path"
     outs = []
     for M, N, K in cases:
         a, b = O.inputs_layer(M, N, K, seed=M)
