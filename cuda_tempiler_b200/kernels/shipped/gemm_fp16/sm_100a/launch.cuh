@@ -135,7 +135,7 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.K = pr.K;
   a.tiles_p = (rows_p + Cfg::BM - 1) / Cfg::BM;
   a.tiles_q = (rows_q + BN - 1) / BN;
-  a.num_kb = (pr.K + Cfg::BK - 1) / Cfg::BK;
+  a.num_kb = (pr.K + Cfg::KS - 1) / Cfg::KS;
   a.splits = std::max(1, std::min(h.splits, a.num_kb));
   const int tiles = a.tiles_p * a.tiles_q;
   a.num_units = tiles * a.splits;
@@ -168,9 +168,9 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
     if (WQ == 0)
       ok &= make_map(&mP, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, 128, SW128);
     else
-      // one 64-byte weight row per dequant thread: the 64-byte swizzle keeps its reads
-      // bank-conflict free
-      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_64B);
+      // one 128-byte row per weight row and request; the 128-byte swizzle keeps the dequant
+      // threads' per-row reads bank-conflict free
+      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, Cfg::KS, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     ok &= make_map(&mQ, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, BN, SW128);
   } else {
     ok &= make_map(&mP, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, SW128);
@@ -184,8 +184,10 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
     // group-wise scale fp16 [K/G][N] and zero uint8 [K/G][N]: one row segment per k-block
     const int wrows = SWAP ? Cfg::BM : BN;
     const uint64_t groups = (uint64_t)(pr.K / pr.group);
-    ok &= make_map(&mS, pr.scale, F16, 2, pr.N, groups, pr.N, wrows, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
-    ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, groups, pr.N, wrows, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const int grows = std::max(1, Cfg::KS / pr.group);  // group rows one stage spans
+    ok &= make_map(&mS, pr.scale, F16, 2, pr.N, groups, pr.N, wrows, grows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, groups, pr.N, wrows, grows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    a.sz_bytes = wrows * 3 * grows;
   }
   if (!ok) return cudaErrorInvalidValue;
 

@@ -43,6 +43,7 @@ struct GemmArgs {
   int group_size;       // group-wise quantisation group along K
   int groups_per_row;   // K / group_size
   int weight_rows;      // N (rows of the weight operand)
+  int sz_bytes;         // group-wise: scale + zero bytes one stage loads
 };
 
 __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -62,33 +63,51 @@ struct SkelCfg {
   static constexpr bool TA = WQ != 0 && SWAP;
   static constexpr int WROWS = WQ ? (SWAP ? BM : BN) : 0;  // rows of the raw weight tile
   static constexpr int P_BYTES = TA ? 0 : BM * BK * 2;
-  static constexpr int Q_BYTES = BN * BK * 2;
-  static constexpr int RAW_BYTES = WROWS * BK;
+  // TA stages cover KS = 128 k: one 128-byte (128B-swizzled) raw row per weight row and TMA
+  // request, and SUB = 2 sub-blocks of 64 k for the MMA.  Every other path: KS = BK = 64.
+  static constexpr int KS = TA ? 128 : BK;
+  static constexpr int SUB = KS / BK;
+  static constexpr int Q_BYTES = BN * KS * 2;  // SUB swizzled atoms of BN x 64 fp16
+  static constexpr int RAW_BYTES = WROWS * KS;
   static constexpr int P_OFF = 0;
   static constexpr int Q_OFF = round_up(P_BYTES, 1024);
   static constexpr int RAW_OFF = Q_OFF + round_up(Q_BYTES, 1024);
   // group-wise: this k-block's scale row (fp16) and zero row (uint8) for the tile's weight rows
-  static constexpr int SZ_BYTES = WQ == 2 ? WROWS * 3 : 0;
+  // (up to SUB group rows per stage: a stage spans KS / group_size groups, group_size >= 64)
+  static constexpr int SZ_BYTES = WQ == 2 ? WROWS * 3 * SUB : 0;
   static constexpr int S_OFF = RAW_OFF + RAW_BYTES;
-  static constexpr int Z_OFF = S_OFF + WROWS * 2;
+  static constexpr int Z_OFF = S_OFF + WROWS * 2 * SUB;
   static constexpr int STAGE_BYTES = RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024);
   static constexpr int EPI_BYTES = SWAP ? 0 : 4 * 2 * 2048;  // per epilogue warp: 2 x [32][32] fp16
-  static constexpr int BAR_BYTES = 512;
-  // TMEM: 2 x BN accumulator columns, plus (TA) 32 columns of fp16 A per stage
-  static constexpr int STAGES =
-      cmin(cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 12),
-           TA ? (512 - 2 * BN) / 32 : 12);
-  static constexpr int A_TMEM_COL = 2 * BN;  // first TMEM column of the A stages (TA)
+  static constexpr int BAR_BYTES = 1024;
+  // TA: a deep shared-memory ring for the raw weight + activation tiles (bytes in flight are
+  // what an HBM-bound decode needs) and a separate, shallower ring of ASLOTS fp16 A slots of
+  // 32 TMEM columns each next to the 2 x BN accumulator columns.  Both counts are even so each
+  // of the two dequant warp groups owns every other stage and every other A slot.
+  static constexpr int SMEM_STAGES = (kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = TA ? cmin(SMEM_STAGES, 24) & ~1 : cmin(SMEM_STAGES, 12);
+  // Independent accumulators per tile: a k-block's four 16-deep UMMAs rotate over NACC
+  // accumulators so that narrow tiles (whose UMMAs are short) are not serialised on the
+  // latency of accumulating into one TMEM region; the epilogue adds them up.
+  static constexpr int NACC = BN <= 32 ? 4 : (BN <= 64 ? 2 : 1);
+  static constexpr int ACC_COLS = NACC * BN;  // TMEM columns of one accumulator buffer
+  static constexpr int ASLOTS = TA ? cmin(8, ((512 - 2 * ACC_COLS) / 32) & ~1) : 1;
+  static constexpr int A_TMEM_COL = 2 * ACC_COLS;  // first TMEM column of the A slots (TA)
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr int NUM_WARPS = 6 + (TA ? 8 : (WQ ? 4 : 0));
   static constexpr int THREADS = NUM_WARPS * 32;
-  static constexpr int TMEM_COLS = TA ? 512 : tmem_cols_for(2 * BN);
+  static constexpr int TMEM_COLS = TA ? 512 : tmem_cols_for(2 * ACC_COLS);
   static constexpr int CW = BN < 32 ? 16 : 32;  // accumulator columns per tcgen05.ld
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
   static_assert(SWAP || BN >= 32, "non-swapped epilogue stores 32-column boxes");
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
-  static_assert(!TA || BN <= 128, "TMEM holds 2 x BN accumulator columns plus the A stages");
-  static_assert(3 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
+  static_assert(!TA || 2 * ACC_COLS + 2 * 32 <= 512, "TMEM: accumulators plus two A slots");
+  static_assert(2 * ACC_COLS <= 512, "TMEM: two accumulator buffers");
+  // barriers: full[STAGES], empty[STAGES], deq[NDEQ] (indexed by stage, or by A slot for TA),
+  // tmem full[2], tmem empty[2], done, aempty[ASLOTS]
+  static constexpr int NDEQ = STAGES > ASLOTS ? STAGES : ASLOTS;
+  static constexpr int NBARS = 2 * STAGES + NDEQ + 5 + ASLOTS;
+  static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
 };
 
 __device__ __forceinline__ void decode_unit(const GemmArgs& a, int unit, int& tile, int& tp,
@@ -119,6 +138,30 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Columns [c*CW, c*CW+CW) of this warp's 32 accumulator rows, summed over the NACC
+// independent accumulators (TMEM -> registers, fp32).
+template <int CW, int NACC, int BN>
+__device__ __forceinline__ void acc_chunk(uint32_t t_acc, int c, float (&f)[32]) {
+  uint32_t v[NACC][32];
+#pragma unroll
+  for (int i = 0; i < NACC; ++i) {
+    if (CW == 32) {
+      tmem_ld_x32(t_acc + i * BN + c * 32, v[i]);
+    } else {
+      uint32_t (&v16)[16] = *reinterpret_cast<uint32_t(*)[16]>(v[i]);
+      tmem_ld_x16(t_acc + i * BN + c * 16, v16);
+    }
+  }
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < CW; ++j) {
+    float a = __uint_as_float(v[0][j]);
+#pragma unroll
+    for (int i = 1; i < NACC; ++i) a += __uint_as_float(v[i][j]);
+    f[j] = a;
+  }
+}
+
 template <int BN, int WQ, bool SWAP>
 __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapQ,
@@ -132,18 +175,22 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
                                              ~uintptr_t(1023));
   uint8_t* epi_smem = smem + STAGES * Cfg::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = abort_flag + 1;
 
   const uint32_t smem_base = smem_u32(smem);
   const uint32_t bar_base = smem_u32(bars);
+  constexpr int kDeq0 = 2 * STAGES, kT0 = kDeq0 + Cfg::NDEQ;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
-  auto deq_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-  auto empty_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + s); };
-  auto tfull_bar = [&](int b) { return bar_base + 8u * (3 * STAGES + b); };
-  auto tempty_bar = [&](int b) { return bar_base + 8u * (3 * STAGES + 2 + b); };
-  const uint32_t done_bar = bar_base + 8u * (3 * STAGES + 4);
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  // deq_bar: dequantised tile of stage s ready, or (TA) A slot s written by 4 quadrant warps
+  auto deq_bar = [&](int s) { return bar_base + 8u * (kDeq0 + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (kT0 + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (kT0 + 2 + b); };
+  const uint32_t done_bar = bar_base + 8u * (kT0 + 4);
+  // TA: aempty_bar(a) = A slot a consumed by the MMAs
+  auto aempty_bar = [&](int a) { return bar_base + 8u * (kT0 + 5 + a); };
   auto p_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::P_OFF; };
   auto q_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::Q_OFF; };
   auto raw_ptr = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_OFF; };
@@ -154,14 +201,16 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(deq_bar(s), Cfg::TA ? 4 : 1);  // TA: 4 quadrant warps; else 1 warp per stage
       mbar_init(empty_bar(s), 1);
     }
+    for (int s = 0; s < Cfg::NDEQ; ++s)
+      mbar_init(deq_bar(s), Cfg::TA ? 4 : 1);  // TA: 4 quadrant warps; else 1 warp per stage
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
       mbar_init(tempty_bar(b), 4);
     }
     mbar_init(done_bar, 1);
+    for (int a = 0; a < Cfg::ASLOTS; ++a) mbar_init(aempty_bar(a), 1);
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -204,18 +253,21 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             ok = false;
             break;
           }
-          const int kx = kb * Cfg::BK;
+          const int kx = kb * Cfg::KS;
           if (WQ == kWFp16) {
             mbar_arrive_expect_tx(full_bar(stage), Cfg::P_BYTES + Cfg::Q_BYTES);
             tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, SWAP ? pol_w : pol_a);
             tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, SWAP ? pol_a : pol_w);
           } else {
             const int wrow0 = SWAP ? tp * Cfg::BM : tq * BN;
-            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + Cfg::SZ_BYTES +
+            mbar_arrive_expect_tx(full_bar(stage), Cfg::RAW_BYTES + args.sz_bytes +
                                                        (SWAP ? Cfg::Q_BYTES : Cfg::P_BYTES));
-            if (SWAP)
-              tma_load_2d(q_addr(stage), &mapQ, full_bar(stage), kx, tq * BN, pol_a);
-            else
+            if (SWAP) {
+#pragma unroll
+              for (int a = 0; a < Cfg::SUB; ++a)
+                tma_load_2d(q_addr(stage) + a * BN * 128, &mapQ, full_bar(stage), kx + a * Cfg::BK,
+                            tq * BN, pol_a);
+            } else
               tma_load_2d(p_addr(stage), &mapP, full_bar(stage), kx, tp * Cfg::BM, pol_a);
             tma_load_2d(smem_u32(raw_ptr(stage)), &mapW, full_bar(stage), kx, wrow0, pol_w);
             if (WQ == kWUint8Group) {
@@ -253,6 +305,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int lu = 0;
+      int it = 0;  // k-block sequence number (A-slot ring position for TA)
       for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x, ++lu) {
         int tile, tp, tq, split, kb0, kb1;
         decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
@@ -260,24 +313,38 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
         const uint32_t uphase = (lu >> 1) & 1;
         if (!mbar_wait(tempty_bar(buf), uphase ^ 1u, abort_flag, 2)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * Cfg::ACC_COLS;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 3)) { ok = false; break; }
-          if (WQ && !mbar_wait(deq_bar(stage), phase, abort_flag, 4)) { ok = false; break; }
+          if (!Cfg::TA && WQ && !mbar_wait(deq_bar(stage), phase, abort_flag, 4)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t pa = p_addr(stage), qa = q_addr(stage);
           if (Cfg::TA) {
-            const uint32_t a_tmem = tmem_base + Cfg::A_TMEM_COL + stage * 32;
+#pragma unroll 1
+            for (int j = 0; j < Cfg::SUB; ++j) {
+              const int aslot = it % Cfg::ASLOTS;
+              const uint32_t aphase = (uint32_t)((it / Cfg::ASLOTS) & 1);
+              ++it;
+              if (!mbar_wait(deq_bar(aslot), aphase, abort_flag, 4)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t a_tmem = tmem_base + Cfg::A_TMEM_COL + aslot * 32;
 #pragma unroll
-            for (int k = 0; k < Cfg::BK / 16; ++k)
-              umma_f16_ts(d_tmem, a_tmem + k * 8, sdesc_k_sw128(qa + k * 32), idesc,
-                          (kb > kb0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < Cfg::BK / 16; ++k)
+                umma_f16_ts(d_tmem + (k % Cfg::NACC) * BN, a_tmem + k * 8,
+                            sdesc_k_sw128(qa + j * BN * 128 + k * 32), idesc,
+                            (kb > kb0 || j > 0 || k >= Cfg::NACC) ? 1u : 0u);
+              umma_commit(aempty_bar(aslot));
+            }
+            if (!ok) break;
           } else {
 #pragma unroll
             for (int k = 0; k < Cfg::BK / 16; ++k) {
-              umma_f16_ss(d_tmem, sdesc_k_sw128(pa + k * 32), sdesc_k_sw128(qa + k * 32), idesc,
-                          (kb > kb0 || k > 0) ? 1u : 0u);
+              umma_f16_ss(d_tmem + (k % Cfg::NACC) * BN, sdesc_k_sw128(pa + k * 32),
+                          sdesc_k_sw128(qa + k * 32), idesc, (kb > kb0 || k >= Cfg::NACC) ? 1u : 0u);
             }
           }
           umma_commit(empty_bar(stage));
@@ -308,7 +375,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
       const uint32_t uphase = (lu >> 1) & 1;
       if (!mbar_wait(tfull_bar(buf), uphase, abort_flag, 5)) break;
       tc_fence_after();
-      const uint32_t t_acc = t_lane + buf * BN;
+      const uint32_t t_acc = t_lane + buf * Cfg::ACC_COLS;
       const int p = tp * Cfg::BM + row;
       const int q0 = tq * BN;
 
@@ -320,9 +387,8 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
         const bool rows_live = tp * Cfg::BM + quad * 32 < args.rows_p;
 #pragma unroll 1
         for (int c = 0; c < nchunk; ++c) {
-          uint32_t v[32];
-          tmem_ld_x32(t_acc + c * 32, v);
-          tmem_wait_ld();
+          float f[32];
+          acc_chunk<32, Cfg::NACC, BN>(t_acc, c, f);
           if (c == nchunk - 1) {
             // accumulator fully read: hand the TMEM buffer back to the MMA warp early
             tc_fence_before();
@@ -330,9 +396,6 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             if (lane == 0) mbar_arrive(tempty_bar(buf));
           }
           if (!rows_live) continue;
-          float f[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
           if (WQ == kWInt8PerChannel) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -367,14 +430,8 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             (WQ == kWInt8PerChannel && p < args.rows_p) ? __half2float(__ldg(args.scale + p)) : 1.f;
 #pragma unroll 1
         for (int c = 0; c < BN / Cfg::CW; ++c) {
-          uint32_t v[32];
-          if (Cfg::CW == 32) {
-            tmem_ld_x32(t_acc + c * 32, v);
-          } else {
-            uint32_t (&v16)[16] = *reinterpret_cast<uint32_t(*)[16]>(v);
-            tmem_ld_x16(t_acc + c * 16, v16);
-          }
-          tmem_wait_ld();
+          float f[32];
+          acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
           if (c == BN / Cfg::CW - 1) {
             tc_fence_before();
             __syncwarp();
@@ -385,7 +442,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             for (int j = 0; j < Cfg::CW; ++j) {
               const int q = q0 + c * Cfg::CW + j;
               if (q < args.rows_q)
-                args.C[(long long)q * args.ldc + p] = __float2half_rn(__uint_as_float(v[j]) * sc);
+                args.C[(long long)q * args.ldc + p] = __float2half_rn(f[j] * sc);
             }
           }
         }
@@ -394,17 +451,11 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
         float* part = args.ws + ((long long)tile * args.splits + split) * (Cfg::BM * BN);
 #pragma unroll 1
         for (int c = 0; c < BN / Cfg::CW; ++c) {
-          uint32_t v[32];
-          if (Cfg::CW == 32) {
-            tmem_ld_x32(t_acc + c * 32, v);
-          } else {
-            uint32_t (&v16)[16] = *reinterpret_cast<uint32_t(*)[16]>(v);
-            tmem_ld_x16(t_acc + c * 16, v16);
-          }
-          tmem_wait_ld();
+          float f[32];
+          acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
 #pragma unroll
           for (int j = 0; j < Cfg::CW; ++j)
-            __stcg(part + (c * Cfg::CW + j) * Cfg::BM + row, __uint_as_float(v[j]));
+            __stcg(part + (c * Cfg::CW + j) * Cfg::BM + row, f[j]);
         }
         tc_fence_before();
         __syncwarp();
@@ -486,60 +537,73 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     // (l >> 2) + 8 j, so its swizzled destination granules are fixed.
     if (Cfg::TA) {
       // Two groups of four warps alternate stages; within a group warp (w & 3) converts the
-      // 32 weight rows of its TMEM lane quadrant, one row per thread: 64 raw bytes (64-byte
-      // swizzled by TMA) -> 32 packed fp16 pairs -> tcgen05.st into the stage's A columns.
+      // 32 weight rows of its TMEM lane quadrant, one row per thread: per 64-k sub-block, 64 raw
+      // bytes -> 32 packed fp16 pairs -> tcgen05.st into one A slot (32 TMEM columns).
       const int grp = (warp - 6) >> 2;
       const int quad = warp & 3;
       const int r = quad * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + Cfg::A_TMEM_COL;
-      int it = 0;
+      const int sw = r & 7;  // 128-byte swizzle: 16-byte granule g of row r lives at g ^ (r & 7)
+      int sit = 0;           // stage-iteration sequence number
       for (int unit = blockIdx.x; unit < args.num_units; unit += gridDim.x) {
         int tile, tp, tq, split, kb0, kb1;
         decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++sit) {
           // a stage always has the same owner, so no owner ever skips one of its phases
-          const int stage = it % STAGES;
+          const int stage = sit % STAGES;
           if ((stage & 1) != grp) continue;
-          const uint32_t phase = (uint32_t)((it / STAGES) & 1);
+          const uint32_t phase = (uint32_t)((sit / STAGES) & 1);
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 6)) { ok = false; break; }
           const uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
-          const uint8_t* raw = sb + Cfg::RAW_OFF + r * 64;
-          const int sw = (r >> 1) & 3;  // 64-byte swizzle: granule j lives at j ^ sw
-          uint4 x[4];
+          const uint8_t* raw = sb + Cfg::RAW_OFF + r * Cfg::KS;
+#pragma unroll 1
+          for (int j = 0; j < Cfg::SUB; ++j) {
+            const int it = sit * Cfg::SUB + j;
+            const int aslot = it % Cfg::ASLOTS;
+            const uint32_t aphase = (uint32_t)((it / Cfg::ASLOTS) & 1);
+            if (!mbar_wait(aempty_bar(aslot), aphase ^ 1u, abort_flag, 7)) { ok = false; break; }
+            tc_fence_after();
+            uint4 x[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) x[j] = *reinterpret_cast<const uint4*>(raw + ((j ^ sw) * 16));
-          __half2 h[32];
-          if (WQ == kWInt8PerChannel) {
-            const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+            for (int u = 0; u < 4; ++u)
+              x[u] = *reinterpret_cast<const uint4*>(raw + (((j * 4 + u) ^ sw) * 16));
+            __half2 h[32];
+            if (WQ == kWInt8PerChannel) {
+              const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              u8x4_to_h2x2_biased(x[j].x ^ 0x80808080u, h[8 * j + 0], h[8 * j + 1]);
-              u8x4_to_h2x2_biased(x[j].y ^ 0x80808080u, h[8 * j + 2], h[8 * j + 3]);
-              u8x4_to_h2x2_biased(x[j].z ^ 0x80808080u, h[8 * j + 4], h[8 * j + 5]);
-              u8x4_to_h2x2_biased(x[j].w ^ 0x80808080u, h[8 * j + 6], h[8 * j + 7]);
+              for (int u = 0; u < 4; ++u) {
+                u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[8 * u + 0], h[8 * u + 1]);
+                u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[8 * u + 2], h[8 * u + 3]);
+                u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[8 * u + 4], h[8 * u + 5]);
+                u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[8 * u + 6], h[8 * u + 7]);
+              }
+#pragma unroll
+              for (int i = 0; i < 32; ++i) h[i] = __hsub2(h[i], bias);
+            } else {
+              // this sub-block's group row inside the stage's scale/zero rows
+              const int gl = (j * Cfg::BK) / args.group_size;
+              const __half2 zb = __half2half2(__ushort_as_half(
+                  (unsigned short)(0x6400u | sb[Cfg::Z_OFF + gl * Cfg::WROWS + r])));
+              const __half2 s2 = __half2half2(
+                  reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[gl * Cfg::WROWS + r]);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                u8x4_to_h2x2_biased(x[u].x, h[8 * u + 0], h[8 * u + 1]);
+                u8x4_to_h2x2_biased(x[u].y, h[8 * u + 2], h[8 * u + 3]);
+                u8x4_to_h2x2_biased(x[u].z, h[8 * u + 4], h[8 * u + 5]);
+                u8x4_to_h2x2_biased(x[u].w, h[8 * u + 6], h[8 * u + 7]);
+              }
+#pragma unroll
+              for (int i = 0; i < 32; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
             }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) h[i] = __hsub2(h[i], bias);
-          } else {
-            const __half2 zb = __half2half2(__ushort_as_half(
-                (unsigned short)(0x6400u | sb[Cfg::Z_OFF + r])));
-            const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[r]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              u8x4_to_h2x2_biased(x[j].x, h[8 * j + 0], h[8 * j + 1]);
-              u8x4_to_h2x2_biased(x[j].y, h[8 * j + 2], h[8 * j + 3]);
-              u8x4_to_h2x2_biased(x[j].z, h[8 * j + 4], h[8 * j + 5]);
-              u8x4_to_h2x2_biased(x[j].w, h[8 * j + 6], h[8 * j + 7]);
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) h[i] = __hmul2(__hsub2(h[i], zb), s2);
+            tmem_st_x32(t_row + aslot * 32, *reinterpret_cast<const uint32_t(*)[32]>(h));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(deq_bar(aslot));
           }
-          tmem_st_x32(t_row + stage * 32, *reinterpret_cast<const uint32_t(*)[32]>(h));
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(deq_bar(stage));
+          if (!ok) break;
         }
         if (!ok) break;
       }

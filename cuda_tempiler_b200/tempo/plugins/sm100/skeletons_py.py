@@ -45,16 +45,18 @@ def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
     """Python mirror of ``SkelCfg<BN, WQ, SWAP>`` in kernel.cuh (shared-memory plan)."""
     ta = bool(wq) and swap  # 8-bit weights dequantised into TMEM as the A operand
     wrows = (BM if swap else bn) if wq else 0
-    p_bytes, q_bytes, raw = (0 if ta else BM * BK * 2), bn * BK * 2, wrows * BK
+    ks = 128 if ta else BK  # k elements per stage
+    p_bytes, q_bytes, raw = (0 if ta else BM * BK * 2), bn * ks * 2, wrows * ks
     q_off = _ru(p_bytes, 1024)
     raw_off = q_off + _ru(q_bytes, 1024)
-    sz = wrows * 3 if wq == 2 else 0
+    sz = wrows * 3 * (ks // BK) if wq == 2 else 0
     stage = raw_off + _ru(raw + sz, 1024)
     epi = 0 if swap else 4 * 2 * 2048
-    bar = 512
-    stages = min((MAX_DYN_SMEM - 1024 - epi - bar) // stage, 12,
-                 (512 - 2 * bn) // 32 if ta else 12)
-    cols = 2 * bn
+    bar = 1024
+    smem_stages = (MAX_DYN_SMEM - 1024 - epi - bar) // stage
+    stages = (min(smem_stages, 24) & ~1) if ta else min(smem_stages, 12)
+    nacc = 4 if bn <= 32 else (2 if bn <= 64 else 1)  # independent accumulators per tile
+    cols = 2 * bn * nacc
     tmem = 512 if ta else (32 if cols <= 32 else 1 << (cols - 1).bit_length())
     return dict(stage_bytes=stage, stages=stages, smem=1024 + stages * stage + epi + bar,
                 threads=32 * (6 + (8 if ta else 4 if wq else 0)), tmem_cols=tmem)

@@ -22,12 +22,29 @@ from ._lib import NotCovered
 HYPER = {"swap": [16, 32, 64, 128], "noswap": [64, 128, 256]}
 
 
+def model_splits(kind, M, N, K, bn, swap):
+    """The k-split the shipped run-time cycle model picks for this hyperform."""
+    import importlib.util
+    import os
+    op = "gemm_fp16" if kind == 0 else "gemm_w8a16"
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "kernels", "shipped", op,
+                     "sm_100a", "select.py")
+    spec = importlib.util.spec_from_file_location("tune_sel_" + op, p)
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m.choose_splits(M, N, K, bn, int(swap), 2 if kind == 0 else 1)
+
+
 class L2Flush:
+    """Evict L2 by READING a 256 MB buffer (written once at set-up): L2 ends up full of clean
+    lines, so the timed kernel never pays for writing back someone else's dirty data."""
+
     def __init__(self, dev, nbytes=256 << 20):
-        self.buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.buf = torch.ones(nbytes // 4, dtype=torch.int32, device=dev)
+        self.out = torch.empty((), dtype=torch.int64, device=dev)
 
     def __call__(self):
-        self.buf.fill_(1)
+        self.out = self.buf.sum()
 
 
 def time_paired(fa, fb, flush, rounds=7):
@@ -64,20 +81,28 @@ def make_problem(kind, M, N, K, dev, g, group=128):
     return dict(A=A, W=W, scale=s, zero=z, group=group, Wref=Wd)
 
 
-def tune_problem(kind, M, N, K, dev, flush, g, rounds=7):
+def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=None):
     p = make_problem(kind, M, N, K, dev, g)
     ref = torch.nn.functional.linear(p["A"], p["Wref"])
     cublas = lambda: torch.nn.functional.linear(p["A"], p["Wref"])
     rows = []
-    cands = [(bn, True) for bn in HYPER["swap"] if M <= 256] + [(bn, False) for bn in HYPER["noswap"]]
+    cands = [(bn, True) for bn in HYPER["swap"] if M <= 256 or kind != 0] + \
+        [(bn, False) for bn in HYPER["noswap"]]
+    if quick:  # only the tiles that can win at this M
+        cands = [(bn, sw) for bn, sw in cands
+                 if (sw and bn >= min(M, 128) and bn <= max(16, 2 * M)) or (not sw and M >= 128)]
     for bn, swap in cands:
         model = ops.select(kind, M, N, K)
         rows_p, rows_q = (N, M) if swap else (M, N)
-        splits_set = {1}
         tiles = -(-rows_p // 128) * -(-rows_q // bn)
-        for s in (2, 3, 4, 6, 8):
-            if tiles * s <= 4 * 148 and s <= K // 128:
-                splits_set.add(s)
+        splits_set = {1}
+        if quick:
+            # the run-time model's k-split for this hyperform
+            splits_set.add(model_splits(kind, M, N, K, bn, swap))
+        else:
+            for s in (2, 3, 4, 6, 8):
+                if tiles * s <= 4 * 148 and s <= K // 128:
+                    splits_set.add(s)
         for splits in sorted(splits_set):
             f = lambda: ops.gemm_hyperform(p["A"], p["W"], bn=bn, swap=swap, splits=splits,
                                            scale=p["scale"], zero=p["zero"], group_size=p["group"])
@@ -111,7 +136,12 @@ def main(argv=None):
     ap.add_argument("--ms", default=None, help="comma-separated M values")
     ap.add_argument("--rounds", type=int, default=5)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--quick", action="store_true", help="model k-split only, plausible tiles only")
+    ap.add_argument("--budget-s", type=float, default=600.0, help="stop after this many seconds")
+    ap.add_argument("--shapes", default=None, help="comma-separated shape names")
     a = ap.parse_args(argv)
+    import time
+    t_start = time.time()
     dev = torch.device("cuda", 0)
     flush = L2Flush(dev)
     g = torch.Generator(device=dev)
@@ -125,8 +155,13 @@ def main(argv=None):
               list(WL.LAYER_FP16_M) if kind == 0 else
               list(WL.W8_PER_CHANNEL_M) if kind == 1 else list(WL.W8_GROUP_M))
         for s in shapes:
+            if a.shapes and s.name not in a.shapes.split(","):
+                continue
             for M in ms:
-                r = tune_problem(kind, M, s.N, s.K, dev, flush, g, a.rounds)
+                if time.time() - t_start > a.budget_s:
+                    print("time budget reached", flush=True)
+                    break
+                r = tune_problem(kind, M, s.N, s.K, dev, flush, g, a.rounds, a.quick)
                 r["name"] = s.name
                 res.append(r)
                 b = r["best"]
