@@ -78,14 +78,19 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
   h.group_m = r->group_m;
   h.max_ctas = 0;
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + h.bn - 1) / h.bn);
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
   const int num_kb = (K + 63) / 64;
+  if (h.bn == 0) {  // streaming GEMV row of the ladder
+    h.splits = 1;
+    return M <= kGemvMaxM;
+  }
   const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
   h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes, hbm);
   return find_inst(wkind, h.bn, h.swap) != nullptr;
 }
 
 cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  if (h.bn == 0) return run_gemv(pr, st);
   const InstEntry* e = find_inst(pr.wkind, h.bn, h.swap);
   if (!e) return cudaErrorInvalidConfiguration;
   return e->fn(pr, h, st);
@@ -142,7 +147,7 @@ size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind) {
   Hyper h{};
   if (!select_hyper(weight_kind, M, N, K, (size_t)1 << 40, h, current_sms())) return 0;
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + h.bn - 1) / h.bn);
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
   return ws_needed(tiles, h.splits, h.bn);
 }
 
@@ -274,7 +279,7 @@ extern "C" int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void*
   if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, current_sms()))
     return cudaErrorInvalidConfiguration;
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + h.bn - 1) / h.bn);
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
   const size_t need = ws_needed(tiles, h.splits, h.bn);
   if (need > (size_t)TEMPO_SM100_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -198,6 +198,39 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Decode-sized streaming GEMV (hyperform bn == 0): M <= 4, 256 threads, R weight rows per warp.
+template <int WQ, int MM, int R>
+cudaError_t launch_gemv(const Problem& pr, cudaStream_t st) {
+  const int rows_per_block = 8 * R;
+  const int grid = (pr.N + rows_per_block - 1) / rows_per_block;
+  k_gemv_sm100<WQ, MM, R><<<grid, 256, 0, st>>>(
+      static_cast<const __half*>(pr.A), static_cast<const uint8_t*>(pr.W),
+      static_cast<const __half*>(pr.scale), static_cast<const uint8_t*>(pr.zero),
+      static_cast<__half*>(pr.C), pr.M, pr.N, pr.K, pr.lda, pr.ldw, pr.ldc,
+      pr.group > 0 ? pr.group : 1);
+  return cudaGetLastError();
+}
+
+template <int WQ, int R>
+cudaError_t gemv_by_m(const Problem& pr, cudaStream_t st) {
+  if (pr.M == 1) return launch_gemv<WQ, 1, R>(pr, st);
+  if (pr.M == 2) return launch_gemv<WQ, 2, R>(pr, st);
+  return launch_gemv<WQ, 4, R>(pr, st);
+}
+
+constexpr int kGemvMaxM = 4;
+
+cudaError_t run_gemv(const Problem& pr, cudaStream_t st) {
+  if (pr.M < 1 || pr.M > kGemvMaxM) return cudaErrorInvalidConfiguration;
+  const bool wide = pr.N >= 9472;  // enough rows for 4 per warp over two waves of 148 SMs
+  switch (pr.wkind) {
+    case 0: return wide ? gemv_by_m<0, 4>(pr, st) : gemv_by_m<0, 2>(pr, st);
+    case 1: return wide ? gemv_by_m<1, 4>(pr, st) : gemv_by_m<1, 2>(pr, st);
+    case 2: return wide ? gemv_by_m<2, 4>(pr, st) : gemv_by_m<2, 2>(pr, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
 using LaunchFn = cudaError_t (*)(const Problem&, const Hyper&, cudaStream_t);
 
 struct InstEntry {

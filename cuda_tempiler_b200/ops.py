@@ -101,7 +101,8 @@ def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, spl
                    group_m: int = 8, max_ctas: int = 0, scale: torch.Tensor | None = None,
                    zero: torch.Tensor | None = None, group_size: int = 0,
                    out: torch.Tensor | None = None) -> torch.Tensor:
-    """Launch one explicit hyperform (search-space point) of the skeleton family."""
+    """Launch one explicit hyperform (search-space point) of the skeleton family; bn=0 is the
+    streaming GEMV (M <= 4)."""
     lib = _lib.load()
     M, K = A.shape
     N = W.shape[0]
@@ -109,7 +110,7 @@ def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, spl
                                                else W8_UINT8_GROUP)
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=A.device)
-    tiles = -(-(N if swap else M) // 128) * -(-(M if swap else N) // bn)
+    tiles = -(-(N if swap else M) // 128) * -(-(M if swap else N) // max(bn, 1))
     nb = 0
     if splits > 1:
         nb = ((tiles * 4 + 255) // 256) * 256 + tiles * splits * 128 * bn * 4

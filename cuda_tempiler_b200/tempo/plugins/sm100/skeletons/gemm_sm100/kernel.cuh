@@ -89,9 +89,10 @@ struct SkelCfg {
   // Independent accumulators per tile: a k-block's four 16-deep UMMAs rotate over NACC
   // accumulators so that narrow tiles (whose UMMAs are short) are not serialised on the
   // latency of accumulating into one TMEM region; the epilogue adds them up.
-  static constexpr int NACC = BN <= 32 ? 4 : (BN <= 64 ? 2 : 1);
+  static constexpr int NACC = TA ? 1 : (BN <= 32 ? 4 : (BN <= 64 ? 2 : 1));
   static constexpr int ACC_COLS = NACC * BN;  // TMEM columns of one accumulator buffer
-  static constexpr int ASLOTS = TA ? cmin(8, ((512 - 2 * ACC_COLS) / 32) & ~1) : 1;
+  // as many A slots as TMEM leaves, a multiple of 2 x SUB (two dequant groups, SUB per stage)
+  static constexpr int ASLOTS = TA ? cmin(16, ((512 - 2 * ACC_COLS) / 32) & ~3) : 1;
   static constexpr int A_TMEM_COL = 2 * ACC_COLS;  // first TMEM column of the A slots (TA)
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr int NUM_WARPS = 6 + (TA ? 8 : (WQ ? 4 : 0));
@@ -682,6 +683,144 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace tempo_sm100
+
+namespace tempo_sm100 {
+
+// ---------------------------------------------------------------------------------------------
+// k_gemv_sm100: the decode-sized (M <= 4) streaming GEMV, C[m][n] = sum_k A[m][k] * W[n][k].
+//
+// At M <= 16 a 128 x N x 16 UMMA costs about as much as a wide one, so the tensor-core path is
+// instruction-bound there; this kernel instead streams each weight row once with 16-byte
+// read-only loads (kept out of L1), dequantises in registers and multiplies on the CUDA cores.
+// Warp w owns R consecutive weight rows; lane l reads 16-byte chunks l, l + 32, ... of each row.
+// Products of one 16-byte chunk are summed in packed fp16 (4 or 8 terms per half), then added
+// to fp32 accumulators; a warp shuffle reduction finishes each (m, row).
+// ---------------------------------------------------------------------------------------------
+template <int WQ>
+__device__ __forceinline__ void gemv_weights(uint4 x, __half2 (&w)[8], __half2 zb, __half2 s2) {
+  if (WQ == kWInt8PerChannel) {
+    const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+    u8x4_to_h2x2_biased(x.x ^ 0x80808080u, w[0], w[1]);
+    u8x4_to_h2x2_biased(x.y ^ 0x80808080u, w[2], w[3]);
+    u8x4_to_h2x2_biased(x.z ^ 0x80808080u, w[4], w[5]);
+    u8x4_to_h2x2_biased(x.w ^ 0x80808080u, w[6], w[7]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = __hsub2(w[i], bias);
+  } else {
+    u8x4_to_h2x2_biased(x.x, w[0], w[1]);
+    u8x4_to_h2x2_biased(x.y, w[2], w[3]);
+    u8x4_to_h2x2_biased(x.z, w[4], w[5]);
+    u8x4_to_h2x2_biased(x.w, w[6], w[7]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = __hmul2(__hsub2(w[i], zb), s2);
+  }
+}
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+template <int WQ, int MM, int R>
+__global__ void __launch_bounds__(256)
+    k_gemv_sm100(const __half* __restrict__ A, const uint8_t* __restrict__ W,
+                 const __half* __restrict__ scale, const uint8_t* __restrict__ zero,
+                 __half* __restrict__ C, int M, int N, int K, long long lda, long long ldw,
+                 long long ldc, int group) {
+  constexpr int ESZ = WQ ? 1 : 2;       // weight bytes per element
+  constexpr int KC = 16 / ESZ;          // k per 16-byte chunk
+  const int lane = threadIdx.x & 31;
+  const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int n0 = warp_g * R;
+  if (n0 >= N) return;
+  const int nchunks = K / KC;           // K % KC == 0 (checked by applicability)
+  float acc[MM][R];
+#pragma unroll
+  for (int m = 0; m < MM; ++m)
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[m][r] = 0.f;
+  const int G = WQ == kWUint8Group ? group : 1;
+#pragma unroll 2
+  for (int c = lane; c < nchunks; c += 32) {
+    const int k0 = c * KC;
+    uint4 x[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int n = min(n0 + r, N - 1);
+      x[r] = ld_stream(W + (long long)n * ldw * ESZ + (long long)c * 16);
+    }
+    __half2 a[MM][KC / 2];
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+      if (m < M) {
+        const uint4* ap = reinterpret_cast<const uint4*>(A + (long long)m * lda + k0);
+#pragma unroll
+        for (int q = 0; q < KC / 8; ++q) {
+          const uint4 v = __ldg(ap + q);
+          a[m][4 * q + 0] = *reinterpret_cast<const __half2*>(&v.x);
+          a[m][4 * q + 1] = *reinterpret_cast<const __half2*>(&v.y);
+          a[m][4 * q + 2] = *reinterpret_cast<const __half2*>(&v.z);
+          a[m][4 * q + 3] = *reinterpret_cast<const __half2*>(&v.w);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < KC / 2; ++q) a[m][q] = __float2half2_rn(0.f);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      __half2 w[8];
+      if (WQ == kWFp16) {
+        w[0] = *reinterpret_cast<const __half2*>(&x[r].x);
+        w[1] = *reinterpret_cast<const __half2*>(&x[r].y);
+        w[2] = *reinterpret_cast<const __half2*>(&x[r].z);
+        w[3] = *reinterpret_cast<const __half2*>(&x[r].w);
+      } else {
+        __half2 zb = __float2half2_rn(0.f), s2 = zb;
+        if (WQ == kWUint8Group) {
+          const int n = min(n0 + r, N - 1);
+          const long long gi = (long long)(k0 / G) * N + n;
+          zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | __ldg(zero + gi))));
+          s2 = __half2half2(__ldg(scale + gi));
+        }
+        gemv_weights<WQ>(x[r], w, zb, s2);
+      }
+#pragma unroll
+      for (int m = 0; m < MM; ++m) {
+        __half2 p = __hmul2(w[0], a[m][0]);
+#pragma unroll
+        for (int q = 1; q < KC / 2; ++q) p = __hfma2(w[q], a[m][q], p);
+        const float2 f = __half22float2(p);
+        acc[m][r] += f.x + f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MM; ++m)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float v = acc[m][r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[m][r] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int n = n0 + r;
+      if (n >= N) break;
+      const float sc = WQ == kWInt8PerChannel ? __half2float(__ldg(scale + n)) : 1.f;
+#pragma unroll
+      for (int m = 0; m < MM; ++m)
+        if (m < M) C[(long long)m * ldc + n] = __float2half_rn(acc[m][r] * sc);
+    }
   }
 }
 

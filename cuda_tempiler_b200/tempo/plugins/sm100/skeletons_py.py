@@ -42,7 +42,10 @@ def _ru(x, a):
 
 
 def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
-    """Python mirror of ``SkelCfg<BN, WQ, SWAP>`` in kernel.cuh (shared-memory plan)."""
+    """Python mirror of ``SkelCfg<BN, WQ, SWAP>`` in kernel.cuh (shared-memory plan);
+    bn == 0 is the streaming GEMV (no shared memory, no TMEM, 256 threads)."""
+    if bn == 0:
+        return dict(stage_bytes=0, stages=0, smem=0, threads=256, tmem_cols=0)
     ta = bool(wq) and swap  # 8-bit weights dequantised into TMEM as the A operand
     wrows = (BM if swap else bn) if wq else 0
     ks = 128 if ta else BK  # k elements per stage
@@ -55,7 +58,7 @@ def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
     bar = 1024
     smem_stages = (MAX_DYN_SMEM - 1024 - epi - bar) // stage
     stages = (min(smem_stages, 24) & ~1) if ta else min(smem_stages, 12)
-    nacc = 4 if bn <= 32 else (2 if bn <= 64 else 1)  # independent accumulators per tile
+    nacc = 1 if ta else (4 if bn <= 32 else (2 if bn <= 64 else 1))  # accumulators per tile
     cols = 2 * bn * nacc
     tmem = 512 if ta else (32 if cols <= 32 else 1 << (cols - 1).bit_length())
     return dict(stage_bytes=stage, stages=stages, smem=1024 + stages * stage + epi + bar,
@@ -106,11 +109,15 @@ def check_op(op) -> int:
 
 
 def key_of(p: dict) -> str:
+    if p["bn"] == 0:
+        return f"gemv_sm100_wq{p['weight']}_m{p['mm']}_r{p['rows']}"
     return (f"{FAMILY}_bn{p['bn']}_sw{p['swap']}_sp{p['splits']}_gm{p['group_m']}"
             f"_wq{p['weight']}_cg{p['cta_group']}")
 
 
 def entry_name(p: dict) -> str:
+    if p["bn"] == 0:
+        return f"tempo_sm100::k_gemv_sm100<{p['weight']}, {p.get('mm', 4)}, {p.get('rows', 4)}>"
     return f"tempo_sm100::k_gemm_sm100<{p['bn']}, {p['weight']}, {'true' if p['swap'] else 'false'}>"
 
 
@@ -161,6 +168,13 @@ class Sm100Skeletons:
         M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
         num_kb = math.ceil(K / BK)
         forms, forms_out = [], []
+        if M <= 4:
+            p = dict(family=FAMILY, bn=0, swap=0, splits=1, group_m=0, weight=wq, stages=0,
+                     cta_group=1, tmem_bufs=0, mm=1 if M == 1 else (2 if M == 2 else 4),
+                     rows=4 if N >= 9472 else 2)
+            if wq == 2:
+                p["group_size"] = group_size(op)
+            forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
         if M <= 256:
             forms += [(bn, 1) for bn in SWAP_BN]
         forms += [(bn, 0) for bn in PREFILL_BN]
@@ -202,8 +216,13 @@ class Sm100Skeletons:
         share of the compulsory HBM traffic, epilogue bytes and dequantised elements."""
         p = h.params
         M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
-        g = problem_geometry(op, p)
         sms = int(self.m.sms().value)
+        if p["bn"] == 0:  # streaming GEMV: HBM stream shared by all SMs, CUDA-core FMAs
+            w_bytes = 1 if p["weight"] else 2
+            hbm = (2.0 * M * K + w_bytes * N * K + 2.0 * M * N) / sms
+            return [Atom(0, AtomKind.MEM_READ, "LDG.128.STREAM", {"HBM": hbm}),
+                    Atom(1, AtomKind.COMPUTE, "HFMA2", {"FMA": 2.0 * M * N * K / sms})]
+        g = problem_geometry(op, p)
         waves = math.ceil(g["units"] / sms)
         kb = waves * g["kb_per_unit"]
         bn, wq = p["bn"], p["weight"]
@@ -234,12 +253,18 @@ class Sm100Skeletons:
     def resources_of(self, op, h):
         p = h.params
         c = skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
-        regs = self._facts.get(entry_name(p), {}).get("regs", 128) + self._staging_regs(p)
+        regs = self._facts.get(entry_name(p), {}).get("regs", 128 if p["bn"] else 64)
+        if p["bn"]:
+            regs += self._staging_regs(p)
         return regs, regs, SmemBytes(c["smem"], c["tmem_cols"])
 
     def launch_of(self, op, h):
         p = h.params
         c = skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+        if p["bn"] == 0:
+            rows = 8 * p["rows"]
+            return Launch(grid_ctas=-(-op.shapes["N"] // rows), threads=256, smem_bytes=0,
+                          entry=entry_name(p), min_ctas_per_sm=1)
         g = problem_geometry(op, p)
         return Launch(grid_ctas=min(g["units"], int(self.m.sms().value)), threads=c["threads"],
                       smem_bytes=c["smem"], entry=entry_name(p), min_ctas_per_sm=1)
@@ -269,7 +294,7 @@ class Sm100Skeletons:
                           "swap_ab", "split_k", "tcgen05", "tma", "persistent"})
 
 
-DEFAULT_LADDER = [(16, 16, 1), (32, 32, 1), (64, 64, 1), (256, 128, 1), (1 << 31, 256, 0)]
+DEFAULT_LADDER = [(4, 0, 0), (16, 16, 1), (32, 32, 1), (64, 64, 1), (256, 128, 1), (1 << 31, 256, 0)]
 
 
 def ladder_pick(op, wq: int):

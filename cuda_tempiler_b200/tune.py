@@ -88,15 +88,20 @@ def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=N
     rows = []
     cands = [(bn, True) for bn in HYPER["swap"] if M <= 256 or kind != 0] + \
         [(bn, False) for bn in HYPER["noswap"]]
+    if M <= 4:
+        cands = [(0, False)] + cands  # the streaming GEMV
     if quick:  # only the tiles that can win at this M
         cands = [(bn, sw) for bn, sw in cands
-                 if (sw and bn >= min(M, 128) and bn <= max(16, 2 * M)) or (not sw and M >= 128)]
+                 if bn == 0 or (sw and bn >= min(M, 128) and bn <= max(16, 2 * M))
+                 or (not sw and M >= 128)]
     for bn, swap in cands:
         model = ops.select(kind, M, N, K)
         rows_p, rows_q = (N, M) if swap else (M, N)
-        tiles = -(-rows_p // 128) * -(-rows_q // bn)
+        tiles = -(-rows_p // 128) * -(-rows_q // max(bn, 1))
         splits_set = {1}
-        if quick:
+        if bn == 0:
+            pass
+        elif quick:
             # the run-time model's k-split for this hyperform
             splits_set.add(model_splits(kind, M, N, K, bn, swap))
         else:

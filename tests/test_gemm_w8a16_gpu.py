@@ -104,3 +104,21 @@ def test_gptq_checkpoint_layout_end_to_end(dev):
     torch.cuda.synchronize()
     ref = a.astype(np.float32) @ d["W"].astype(np.float32)
     assert O.rel_l2(C.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("N,K", [(272, 512), (10240, 1024), (9472, 2064)])
+def test_streaming_gemv(dev, M, N, K):
+    """The CUDA-core streaming GEMV (hyperform bn=0, M <= 4) for all three weight kinds."""
+    from cuda_tempiler_b200 import ops
+    r1 = _pc(M, N, K, lambda A, W, s, C: ops.gemm_hyperform(A, W, bn=0, swap=False, scale=s, out=C))
+    G = 128 if K % 128 == 0 else 64 if K % 64 == 0 else 16
+    if K % 64 == 0:
+        r2 = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+            A, W, bn=0, swap=False, scale=s, zero=z, group_size=G, out=C), G=128 if K % 128 == 0 else 64)
+        assert r2 <= TOL, r2
+    a, b = O.inputs_layer(M, N, K, seed=M)
+    C = ops.gemm_hyperform(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), bn=0, swap=False)
+    torch.cuda.synchronize()
+    r3 = O.rel_l2(C.cpu().numpy(), O.gemm_fp16_ref(a, b))
+    assert r1 <= TOL and r3 <= TOL, (r1, r3)

@@ -50,7 +50,8 @@ def test_frozen_kernel_equals_skeleton(op):
 
 def test_select_predicate_and_fallback():
     s16, s8 = load_select("gemm_fp16"), load_select("gemm_w8a16")
-    assert s16.select("gemm_fp16", 1, 4096, 3840)["swap"] == 1
+    assert s16.select("gemm_fp16", 1, 4096, 3840)["bn"] == 0           # streaming GEMV
+    assert s16.select("gemm_fp16", 8, 4096, 3840)["swap"] == 1
     assert s16.select("gemm_fp16", 4096, 15360, 3840)["bn"] == 256
     assert s16.select("gemm_fp16", 4, 4095, 3840) is None        # N % 8: not covered -> fallback
     assert s16.select("gemm_fp16", 4, 4096, 3840, arch="sm_70") is None
