@@ -34,6 +34,10 @@ EXPORTS = {
     "tempo_sm100_gemm_hyperform": (
         _i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
              _vp, _sz, _vp]),
+    "tempo_sm100_gemm_hyperform_cg": (
+        _i, [_i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i,
+             _vp, _sz, _vp]),
+    "tempo_sm100_pair_resources": (_i, [_i, _ip]),
     "tempo_sm100_select": (_i, [_i, _i, _i, _i, _sz, _ip]),
     "tempo_sm100_hyperform_resources": (_i, [_i, _i, _i, _ip]),
     "tempo_sm100_naive_gemm_fp16": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),

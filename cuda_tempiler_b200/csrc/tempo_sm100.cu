@@ -21,6 +21,7 @@ namespace {
 struct LadderRow {
   int m_max;  // inclusive upper bound on M (0x7fffffff = everything else)
   int bn, swap, group_m;
+  int cta_group;  // 1, or 2 for the 2-CTA 256 x BN prefill tiles (fp16)
 };
 
 #include "gemm_fp16/sm_100a/dispatch.inc"
@@ -77,12 +78,17 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
   h.swap = r->swap;
   h.group_m = r->group_m;
   h.max_ctas = 0;
+  h.cta_group = (wkind == 0 && r->cta_group == 2 && !r->swap) ? 2 : 1;
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
   const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
   const int num_kb = (K + 63) / 64;
   if (h.bn == 0) {  // streaming GEMV row of the ladder
     h.splits = 1;
     return M <= kGemvMaxM;
+  }
+  if (h.cta_group == 2) {  // pair tiles: no split-K
+    h.splits = 1;
+    return true;
   }
   const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
   h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes, hbm);
@@ -91,6 +97,7 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
 
 cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
   if (h.bn == 0) return run_gemv(pr, st);
+  if (h.cta_group == 2) return run_pair(pr, h, st);
   const InstEntry* e = find_inst(pr.wkind, h.bn, h.swap);
   if (!e) return cudaErrorInvalidConfiguration;
   return e->fn(pr, h, st);
@@ -165,6 +172,25 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
   Problem pr{weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
   return run(pr, h, static_cast<cudaStream_t>(stream));
 }
+
+int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W, const void* scale,
+                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                                  int ldc, int group_size, int bn, int swap, int splits,
+                                  int group_m, int max_ctas, int cta_group, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  if (cta_group != 2)
+    return tempo_sm100_gemm_hyperform(weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc,
+                                      group_size, bn, swap, splits, group_m, max_ctas, ws, ws_bytes,
+                                      stream);
+  if (weight_kind != 0 || swap || splits > 1) return cudaErrorInvalidConfiguration;
+  if (!fp16_applicable(A, W, C, M, N, K, lda, ldw, ldc)) return cudaErrorInvalidConfiguration;
+  Hyper h{bn, 0, 1, group_m < 1 ? 1 : group_m, max_ctas};
+  h.cta_group = 2;
+  Problem pr{0, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
+  return run(pr, h, static_cast<cudaStream_t>(stream));
+}
+
+int tempo_sm100_pair_resources(int bn, int* out6) { return pair_resources(bn, out6); }
 
 int tempo_sm100_select(int weight_kind, int M, int N, int K, size_t ws_bytes, int* out5) {
   Hyper h{};

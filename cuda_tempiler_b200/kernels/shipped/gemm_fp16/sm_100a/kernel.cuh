@@ -261,6 +261,111 @@ __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // ---------------------------------------------------------------------------------------
+// Clusters and the 2-SM (cta_group::2) forms.  No TMA load here is a cluster-broadcast load:
+// each CTA of a pair loads its own operand halves; only tcgen05.commit multicasts.
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (arrivals may come from the peer CTA).
+__device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, int where) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      if (atomicCAS(&g_status[0], 0, 1) == 0) {
+        g_status[1] = where;
+        g_status[2] = blockIdx.x;
+      }
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// Arrive on an mbarrier that may live in the peer CTA (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completion is counted on `bar`, which may
+// be the leader CTA's barrier (shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int x, int y, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(cache_hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[both CTAs' smem] * B[both CTAs' smem]^T, M = 256 over the pair.
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` (same offset) in every CTA of `mask` when this thread's prior tcgen05 ops end.
+__device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte
@@ -1120,6 +1225,237 @@ __global__ void __launch_bounds__(256)
       for (int m = 0; m < MM; ++m)
         if (m < M) C[(long long)m * ldc + n] = __float2half_rn(acc[m][r] * sc);
     }
+  }
+}
+
+}  // namespace tempo_sm100
+
+namespace tempo_sm100 {
+
+// ---------------------------------------------------------------------------------------------
+// k_gemm_sm100_pair: fp16 prefill tiles of 256 x BN on a 2-CTA cluster (cta_group::2).
+//
+// CTA r of the pair holds A rows [256 t + 128 r, +128) and B rows [BN u + (BN/2) r, +BN/2) of
+// every k-block, loaded by its own TMA (no multicast); the leader (rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, which reads both CTAs' shared memory and writes each
+// CTA's own 128 x BN accumulator in its TMEM.  Per SM this halves the B feed of the 1-CTA
+// 128 x BN tile.  Stage completion: both CTAs' TMA bytes are counted on the leader's full
+// barrier; tcgen05.commit multicasts stage release and accumulator-ready to both CTAs; both
+// epilogues report accumulator-consumed to the leader.  Non-swapped, no split-K.
+// ---------------------------------------------------------------------------------------------
+template <int BN_>
+struct PairCfg {
+  static constexpr int BM = 128, BN = BN_, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int B_OFF = A_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + round_up(B_BYTES, 1024);
+  static constexpr int EPI_BYTES = 4 * 2 * 2048;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int STAGES = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 8);
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 192;
+  static constexpr int TMEM_COLS = tmem_cols_for(2 * BN);
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
+    k_gemm_sm100_pair(const __grid_constant__ CUtensorMap mapA,
+                      const __grid_constant__ CUtensorMap mapB,
+                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
+  using Cfg = PairCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t done_bar = bar_base + 8u * (2 * STAGES + 4);
+  auto a_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES; };
+  auto b_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::B_OFF; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // leader: its own arrive.expect_tx + both CTAs' bytes
+      mbar_init(empty_bar(s), 1);  // multicast commit from the leader's MMA thread
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 8);  // leader: 4 epilogue warps of each CTA
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapB);
+    tma_prefetch_desc(&mapC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both)
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int unit = cluster; unit < args.num_units; unit += nclusters) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, 11)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+          const uint32_t lead_full = mapa_shared(full_bar(stage), 0);
+          const int kx = kb * Cfg::BK;
+          tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
+          tma_load_2d_pair(b_addr(stage), &mapB, lead_full, kx, tq * BN + (int)rank * (BN / 2), pol);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain: the leader's full barriers see every byte both CTAs requested.
+      if (leader) {
+        const int pending = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < pending; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1u;
+          }
+          mbar_drain(full_bar(s), ph, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int lu = 0;
+      for (int unit = cluster; unit < args.num_units; unit += nclusters, ++lu) {
+        int tile, tp, tq, split, kb0, kb1;
+        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+        const int buf = lu & 1;
+        const uint32_t uphase = (lu >> 1) & 1;
+        if (!mbar_wait_cluster(tempty_bar(buf), uphase ^ 1u, abort_flag, 12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, 13)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k)
+            umma_f16_ss_pair(d_tmem, sdesc_k_sw128(a_addr(stage) + k * 32),
+                             sdesc_k_sw128(b_addr(stage) + k * 32), idesc,
+                             (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_mc(empty_bar(stage), 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(tfull_bar(buf), 0x3);
+      }
+      umma_commit_pair_mc(done_bar, 0x1);
+      mbar_drain(done_bar, 0, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both)
+    const int quad = warp & 3;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+    uint8_t* stage_buf = epi_smem + (warp - 2) * 4096;
+    int sb = 0;
+    int lu = 0;
+    for (int unit = cluster; unit < args.num_units; unit += nclusters, ++lu) {
+      int tile, tp, tq, split, kb0, kb1;
+      decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+      const int buf = lu & 1;
+      const uint32_t uphase = (lu >> 1) & 1;
+      if (!mbar_wait(tfull_bar(buf), uphase, abort_flag, 14)) break;
+      tc_fence_after();
+      const uint32_t t_acc = t_lane + buf * BN;
+      const int q0 = tq * BN;
+      const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
+      const int live_cols = args.rows_q - q0;
+      const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
+      const bool rows_live = row0 < args.rows_p;
+#pragma unroll 1
+      for (int c = 0; c < nchunk; ++c) {
+        float f[32];
+        acc_chunk<32, 1, BN>(t_acc, c, f);
+        if (c == nchunk - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+        }
+        if (!rows_live) continue;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* sbuf = stage_buf + sb * 2048;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          w.x = pack_half2(f[8 * g + 0], f[8 * g + 1]);
+          w.y = pack_half2(f[8 * g + 2], f[8 * g + 3]);
+          w.z = pack_half2(f[8 * g + 4], f[8 * g + 5]);
+          w.w = pack_half2(f[8 * g + 6], f[8 * g + 7]);
+          const int pg = g ^ ((lane >> 1) & 3);  // 64-byte swizzle
+          *reinterpret_cast<uint4*>(sbuf + lane * 64 + pg * 16) = w;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&mapC, smem_u32(sbuf), q0 + c * 32, row0);
+          bulk_commit_group();
+        }
+        sb ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers or smem
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

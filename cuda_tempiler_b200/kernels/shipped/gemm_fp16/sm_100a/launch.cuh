@@ -94,6 +94,7 @@ struct Problem {
 
 struct Hyper {
   int bn, swap, splits, group_m, max_ctas;
+  int cta_group = 1;  // 2: 256 x BN tiles on a 2-CTA cluster (fp16 prefill only)
 };
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -254,6 +255,88 @@ const InstEntry kInst[] = {
     TEMPO_INST_WQ(128, true), TEMPO_INST_WQ(64, false),  TEMPO_INST_WQ(128, false),
     TEMPO_INST_WQ(256, false),
 };
+
+// 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs.
+template <int BN>
+cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  using Cfg = PairCfg<BN>;
+  auto kern = k_gemm_sm100_pair<BN>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [&] {
+      attr_err[dev] =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    });
+    if (attr_err[dev] != cudaSuccess) return attr_err[dev];
+  }
+  if (pr.wkind != 0 || h.swap || h.splits > 1) return cudaErrorInvalidConfiguration;
+  GemmArgs a{};
+  a.rows_p = pr.M;
+  a.rows_q = pr.N;
+  a.K = pr.K;
+  a.tiles_p = (pr.M + 255) / 256;
+  a.tiles_q = (pr.N + BN - 1) / BN;
+  a.num_kb = (pr.K + Cfg::BK - 1) / Cfg::BK;
+  a.splits = 1;
+  a.num_units = a.tiles_p * a.tiles_q;
+  a.group_m = std::max(1, h.group_m / 2);  // raster groups counted in 256-row tiles
+  a.C = static_cast<__half*>(pr.C);
+  a.ldc = pr.ldc;
+  a.weight_rows = pr.N;
+  CUtensorMap mA, mB, mC;
+  std::memset(&mA, 0, sizeof(mA));
+  std::memset(&mB, 0, sizeof(mB));
+  std::memset(&mC, 0, sizeof(mC));
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  bool ok = make_map(&mA, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+  ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok) return cudaErrorInvalidValue;
+  const int sms = dev_info(dev).sms;
+  const int max_clusters = std::max(1, (h.max_ctas > 0 ? h.max_ctas : sms) / 2);
+  const int clusters = std::min(a.num_units, max_clusters);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mC, a);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  if (h.bn == 256) return launch_pair<256>(pr, h, st);
+  if (h.bn == 128) return launch_pair<128>(pr, h, st);
+  return cudaErrorInvalidConfiguration;
+}
+
+int pair_resources(int bn, int* out6) {
+  const void* kern = bn == 256 ? reinterpret_cast<const void*>(&k_gemm_sm100_pair<256>)
+                   : bn == 128 ? reinterpret_cast<const void*>(&k_gemm_sm100_pair<128>) : nullptr;
+  if (!kern) return cudaErrorInvalidConfiguration;
+  cudaFuncAttributes fa{};
+  const cudaError_t err = cudaFuncGetAttributes(&fa, kern);
+  out6[0] = 192;
+  out6[1] = bn == 256 ? PairCfg<256>::SMEM : PairCfg<128>::SMEM;
+  out6[2] = bn == 256 ? PairCfg<256>::STAGES : PairCfg<128>::STAGES;
+  out6[3] = bn == 256 ? PairCfg<256>::TMEM_COLS : PairCfg<128>::TMEM_COLS;
+  out6[4] = err == cudaSuccess ? fa.numRegs : -1;
+  out6[5] = err == cudaSuccess ? (int)fa.localSizeBytes : -1;
+  return err;
+}
 
 const InstEntry* find_inst(int wkind, int bn, int swap) {
   for (const auto& e : kInst)

@@ -98,7 +98,8 @@ def gemm_w8a16(A: torch.Tensor, W: torch.Tensor, scale: torch.Tensor,
 
 
 def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, splits: int = 1,
-                   group_m: int = 8, max_ctas: int = 0, scale: torch.Tensor | None = None,
+                   group_m: int = 8, max_ctas: int = 0, cta_group: int = 1,
+                   scale: torch.Tensor | None = None,
                    zero: torch.Tensor | None = None, group_size: int = 0,
                    out: torch.Tensor | None = None) -> torch.Tensor:
     """Launch one explicit hyperform (search-space point) of the skeleton family; bn=0 is the
@@ -115,10 +116,10 @@ def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, spl
     if splits > 1:
         nb = ((tiles * 4 + 255) // 256) * 256 + tiles * splits * 128 * bn * 4
     ws = workspace(A.device, nb)
-    rc = lib.tempo_sm100_gemm_hyperform(
+    rc = lib.tempo_sm100_gemm_hyperform_cg(
         kind, _ptr(A), _ptr(W), _ptr(scale), _ptr(zero), _ptr(out), M, N, K, A.stride(0),
         W.stride(0), out.stride(0), group_size, bn, int(swap), splits, group_m, max_ctas,
-        _ptr(ws), 0 if ws is None else ws.numel(), _stream(A.device))
+        cta_group, _ptr(ws), 0 if ws is None else ws.numel(), _stream(A.device))
     _lib.check(rc, f"hyperform bn={bn} swap={swap} splits={splits}")
     return out
 

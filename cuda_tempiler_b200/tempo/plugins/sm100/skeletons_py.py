@@ -41,6 +41,15 @@ def _ru(x, a):
     return (x + a - 1) // a * a
 
 
+def pair_cfg(bn: int) -> dict:
+    """Python mirror of ``PairCfg<BN>`` (2-CTA 256 x BN tiles, per CTA)."""
+    stage = BM * BK * 2 + _ru((bn // 2) * BK * 2, 1024)
+    epi, bar = 4 * 2 * 2048, 512
+    stages = min((MAX_DYN_SMEM - 1024 - epi - bar) // stage, 8)
+    return dict(stage_bytes=stage, stages=stages, smem=1024 + stages * stage + epi + bar,
+                threads=192, tmem_cols=2 * bn)
+
+
 def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
     """Python mirror of ``SkelCfg<BN, WQ, SWAP>`` in kernel.cuh (shared-memory plan);
     bn == 0 is the streaming GEMV (no shared memory, no TMEM, 256 threads)."""
@@ -116,15 +125,20 @@ def key_of(p: dict) -> str:
 
 
 def entry_name(p: dict) -> str:
+    if p.get("cta_group", 1) == 2:
+        return f"tempo_sm100::k_gemm_sm100_pair<{p['bn']}>"
     if p["bn"] == 0:
         return f"tempo_sm100::k_gemv_sm100<{p['weight']}, {p.get('mm', 4)}, {p.get('rows', 4)}>"
     return f"tempo_sm100::k_gemm_sm100<{p['bn']}, {p['weight']}, {'true' if p['swap'] else 'false'}>"
 
 
 def problem_geometry(op, p):
+    """Units per SM-sized work item; a 2-CTA tile counts as two 128-row units."""
     M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
     rows_p, rows_q = (N, M) if p["swap"] else (M, N)
     tiles = math.ceil(rows_p / BM) * math.ceil(rows_q / p["bn"])
+    if p.get("cta_group", 1) == 2:
+        tiles = 2 * math.ceil(M / 256) * math.ceil(N / p["bn"])
     num_kb = math.ceil(K / BK)
     splits = max(1, min(p["splits"], num_kb))
     return dict(tiles=tiles, num_kb=num_kb, splits=splits, units=tiles * splits,
@@ -178,6 +192,12 @@ class Sm100Skeletons:
         if M <= 256:
             forms += [(bn, 1) for bn in SWAP_BN]
         forms += [(bn, 0) for bn in PREFILL_BN]
+        if wq == 0 and M > 128:  # 2-CTA cluster tiles (cta_group::2), no split-K
+            for bn in (256, 128):
+                c = pair_cfg(bn)
+                p = dict(family=FAMILY, bn=bn, swap=0, splits=1, group_m=16, weight=0,
+                         stages=c["stages"], cta_group=2, tmem_bufs=2)
+                forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
         for bn, swap in forms:
             for splits in SPLITS:
                 if splits > 1 and splits > num_kb // 2:
@@ -192,7 +212,8 @@ class Sm100Skeletons:
         # Most promising first (a pipeline that emits the first kept variant gets the measured
         # ladder's pick): ladder (bn, swap) match, then the plugin's own cycle estimate.
         pick = ladder_pick(op, wq)
-        forms_out.sort(key=lambda h: (0 if pick and (h.params["bn"], h.params["swap"]) == pick else 1,
+        forms_out.sort(key=lambda h: (0 if pick and (h.params["bn"], h.params["swap"],
+                                                     h.params.get("cta_group", 1)) == pick else 1,
                                       self._estimate_cycles(op, h), h.params["splits"], h.key))
         yield from forms_out
 
@@ -227,9 +248,12 @@ class Sm100Skeletons:
         kb = waves * g["kb_per_unit"]
         bn, wq = p["bn"], p["weight"]
         flops = kb * 2.0 * BM * bn * BK
-        smem_rd = kb * (BM + bn) * BK * 2.0
+        b_rows = bn // 2 if p.get("cta_group", 1) == 2 else bn  # B rows this SM holds
+        smem_rd = kb * (BM + b_rows) * BK * 2.0
         w_rows = BM if p["swap"] else bn
         act_rows = bn if p["swap"] else BM
+        if p.get("cta_group", 1) == 2:
+            w_rows = b_rows
         tma = kb * (act_rows * BK * 2.0 + w_rows * BK * (1.0 if wq else 2.0))
         w_bytes = 1 if wq else 2
         hbm_total = 2.0 * M * K + w_bytes * N * K + 2.0 * M * N
@@ -252,7 +276,8 @@ class Sm100Skeletons:
 
     def resources_of(self, op, h):
         p = h.params
-        c = skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+        c = pair_cfg(p["bn"]) if p.get("cta_group", 1) == 2 else \
+            skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
         regs = self._facts.get(entry_name(p), {}).get("regs", 128 if p["bn"] else 64)
         if p["bn"]:
             regs += self._staging_regs(p)
@@ -260,7 +285,8 @@ class Sm100Skeletons:
 
     def launch_of(self, op, h):
         p = h.params
-        c = skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+        c = pair_cfg(p["bn"]) if p.get("cta_group", 1) == 2 else \
+            skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
         if p["bn"] == 0:
             rows = 8 * p["rows"]
             return Launch(grid_ctas=-(-op.shapes["N"] // rows), threads=256, smem_bytes=0,
@@ -309,10 +335,11 @@ def ladder_pick(op, wq: int):
         spec = importlib.util.spec_from_file_location(f"tempo_ship_ladder_{name}", path)
         mod = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(mod)
-        rows = [(r[0], r[1], r[2]) for r in mod.LADDER]
-    for m_max, bn, swap in rows:
-        if M <= m_max:
-            return (bn, swap)
+        rows = [(r[0], r[1], r[2], r[4] if len(r) > 4 else 1) for r in mod.LADDER]
+    for row in rows:
+        if M <= row[0]:
+            cg = row[3] if len(row) > 3 else 1
+            return (row[1], row[2], cg if wq == 0 else 1)
     return None
 
 

@@ -74,6 +74,19 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
                                int ldc, int group_size, int bn, int swap, int splits, int group_m,
                                int max_ctas, void* ws, size_t ws_bytes, void* stream);
 
+/* As tempo_sm100_gemm_hyperform with the cluster axis: cta_group 2 runs fp16 prefill tiles of
+ * 256 x bn (bn 128 or 256) on 2-CTA clusters with tcgen05.mma.cta_group::2 (weight_kind 0,
+ * swap 0, splits 1 only); cta_group 1 is tempo_sm100_gemm_hyperform. */
+int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W, const void* scale,
+                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                                  int ldc, int group_size, int bn, int swap, int splits,
+                                  int group_m, int max_ctas, int cta_group, void* ws,
+                                  size_t ws_bytes, void* stream);
+
+/* Resource facts of the 2-CTA instantiation k_gemm_sm100_pair<bn>, laid out as
+ * tempo_sm100_hyperform_resources' out6 (per CTA). */
+int tempo_sm100_pair_resources(int bn, int* out6);
+
 /* The dispatcher's choice for a problem: out[0..4] = bn, swap, splits, group_m, stages.
  * Returns 9 if the problem is not covered. */
 int tempo_sm100_select(int weight_kind, int M, int N, int K, size_t ws_bytes, int* out5);

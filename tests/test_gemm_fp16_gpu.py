@@ -99,3 +99,28 @@ def test_workspace_left_zero(dev):
     assert int(ws[: tiles * 4].view(torch.int32).abs().sum()) == 0
     assert O.rel_l2(C.cpu().numpy(), O.gemm_fp16_ref(a, b)) <= TOL
     assert ops.device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("M,N,K", [(260, 784, 1032), (1000, 1000, 520), (640, 768, 4096),
+                                   (4096, 15360, 3840)])
+def test_pair_tiles_cta_group2(dev, bn, M, N, K):
+    """256 x bn tiles on 2-CTA clusters (tcgen05.mma.cta_group::2)."""
+    from cuda_tempiler_b200 import ops
+    a, b, c = _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=bn, swap=False, cta_group=2,
+                                                         out=out), M, N, K)
+    _gate(a, b, c)
+    assert ops.device_status() == [0, 0, 0, 0]
+
+
+def test_pair_resources_match_python_plan(dev):
+    import ctypes as C
+    from cuda_tempiler_b200 import _lib
+    from cuda_tempiler_b200.tempo.plugins.sm100.skeletons_py import pair_cfg
+    lib = _lib.load()
+    for bn in (128, 256):
+        out = (C.c_int * 6)()
+        assert lib.tempo_sm100_pair_resources(bn, out) == 0
+        c = pair_cfg(bn)
+        assert (out[0], out[1], out[2], out[3]) == (c["threads"], c["smem"], c["stages"], c["tmem_cols"])
+        assert out[5] == 0

@@ -36,8 +36,8 @@ def test_manifest_signs_every_file(op):
 def test_dispatch_matches_select(op):
     sel = load_select(op)
     inc = open(os.path.join(ROOT, op, "sm_100a", "dispatch.inc")).read()
-    rows = re.findall(r"\{(0x7fffffff|\d+), (\d+), (\d+), (\d+)\}", inc)
-    got = [[int(a, 0), int(b), int(c), int(d)] for a, b, c, d in rows]
+    rows = re.findall(r"\{(0x7fffffff|\d+), (\d+), (\d+), (\d+), (\d+)\}", inc)
+    got = [[int(a, 0), int(b), int(c), int(d), int(e)] for a, b, c, d, e in rows]
     assert got == [list(r) for r in sel.LADDER]
     assert sel.LADDER[-1][0] >= 0x7FFFFFFF, "the last ladder row must cover every M"
 
