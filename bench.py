@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-bars", action="store_true", help="skip cuBLAS/naive/CPU side measurements")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP section")
     ap.add_argument("--case", default=None,
                     help="profiling case NAME:M[:kind] (e.g. gate_up:4096, gate_up:1:w8pc): launch "
                          "that one GEMM warmup+steps times and print its event timing")
@@ -228,6 +229,53 @@ def run_case(args):
                       "gbs": by / t / 1e9, "cfg": ops.select(0 if kind == "fp16" else
                                                              (1 if kind == "w8pc" else 2), M, N, K)}))
     return 0
+
+
+# ------------------------------------------------------------------------------ config 5
+def tp_mlp_block(dev, world, rank, barrier):
+    """BASELINE config 5 on `world` GPUs: W8A16 (int8 per-channel) SwiGLU MLP of the 27B-class
+    layer (H 5120, FFN 17408), gate_up column-parallel, down row-parallel, one NCCL all-reduce.
+    Whole-job TFLOP/s = 6 M H I / (max over ranks of the device time per forward)."""
+    import torch
+    import torch.distributed as dist
+
+    from cuda_tempiler_b200 import tp
+    from cuda_tempiler_b200 import workloads as WL
+    H, I = 5120, 17408
+    if I % world:
+        return []
+    Ir = I // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    sh = tp.MLPShard(
+        w_gate_up=torch.randint(-127, 128, (2 * Ir, H), generator=g, device=dev, dtype=torch.int8),
+        s_gate_up=(torch.rand(2 * Ir, generator=g, device=dev) * 2e-4 + 5e-5).half(),
+        w_down=torch.randint(-127, 128, (H, Ir), generator=g, device=dev, dtype=torch.int8),
+        s_down=(torch.rand(H, generator=g, device=dev) * 2e-4 + 5e-5).half(), inter=Ir)
+    rows = []
+    for M in WL.TP_MLP_M:
+        x = torch.randn(M, H, generator=g, device=dev).half()
+        for _ in range(3):
+            tp.mlp_forward(x, sh)
+        torch.cuda.synchronize()
+        barrier()
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            tp.mlp_forward(x, sh)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        fl = 6.0 * M * H * I
+        rows.append({"M": M, "tp": world, "us": round(ms * 1e3, 1),
+                     "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                     "weight_gbs": round(3.0 * H * I / (ms * 1e-3) / 1e9, 0)})
+    return rows
 
 
 # ------------------------------------------------------------------------------ our arm
@@ -410,6 +458,9 @@ def main():
             "cfg": ops.select(0, M, N, K, ws.numel()),
         })
 
+    # ---- tensor-parallel W8A16 MLP, tp = world size (reported beside)
+    tp_rows = [] if args.no_tp else tp_mlp_block(dev, world, rank, barrier)
+
     # ---- roofline of the dominant kernel
     dom = max(range(n), key=lambda i: per_ms[i])
     x = gemms[dom]
@@ -468,6 +519,7 @@ def main():
         "roofline": roof,
         "cpu_baseline": cpu,
         "per_gemm": per_gemm,
+        "tp_mlp": tp_rows,
         "x_cublas_median": statistics.median(p["x_cublas"] for p in per_gemm) if per_gemm and per_gemm[0]["x_cublas"] else None,
     }
     if rank == 0:

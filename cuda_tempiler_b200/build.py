@@ -33,7 +33,7 @@ def nvcc() -> str:
 
 
 def sources() -> list:
-    return (sorted(CSRC.glob("*.cu")) + sorted(SHIPPED.glob("*/sm_100a/*.cuh"))
+    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(SHIPPED.glob("*/sm_100a/*.cuh"))
             + sorted(SHIPPED.glob("*/sm_100a/*.inc")) + [INCLUDE / "tempo_sm100.h"])
 
 

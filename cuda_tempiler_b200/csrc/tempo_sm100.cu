@@ -14,6 +14,7 @@
 
 #include "tempo_sm100.h"
 #include "launch.cuh"
+#include "elementwise.cuh"
 
 namespace tempo_sm100 {
 namespace {
@@ -243,6 +244,15 @@ int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale
                             static_cast<const __half*>(scale), static_cast<const uint8_t*>(zero),
                             static_cast<__half*>(C), M, N, K, lda, ldw, ldc, quant_kind,
                             group_size, static_cast<cudaStream_t>(stream));
+}
+
+int tempo_sm100_silu_mul(const void* gu, void* out, int M, int I, int ld_gu, int ld_out,
+                         void* stream) {
+  if (M <= 0 || I <= 0 || (I % 8) || (ld_gu % 8) || (ld_out % 8) || ld_gu < 2 * I || ld_out < I)
+    return cudaErrorInvalidValue;
+  if (!aligned16(gu) || !aligned16(out)) return cudaErrorInvalidValue;
+  return launch_silu_mul(static_cast<const __half*>(gu), static_cast<__half*>(out), M, I, ld_gu,
+                         ld_out, static_cast<cudaStream_t>(stream));
 }
 
 int tempo_sm100_device_status(int* out4, int reset) {

@@ -163,3 +163,17 @@ def device_status(reset: bool = True) -> list:
     rc = lib.tempo_sm100_device_status(out, int(reset))
     _lib.check(rc, "device_status")
     return list(out)
+
+
+def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU step: gu [M, 2I] holds [gate | up]; returns silu(gate) * up as [M, I] fp16."""
+    lib = _lib.load()
+    _check_2d(gu, "gu", torch.float16)
+    M, I2 = gu.shape
+    I = I2 // 2
+    if out is None:
+        out = torch.empty((M, I), dtype=torch.float16, device=gu.device)
+    rc = lib.tempo_sm100_silu_mul(_ptr(gu), _ptr(out), M, I, gu.stride(0), out.stride(0),
+                                  _stream(gu.device))
+    _lib.check(rc, "tempo_sm100_silu_mul")
+    return out

@@ -104,6 +104,12 @@ int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale
                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
                                  int ldc, int quant_kind, int group_size, void* stream);
 
+/* out[m][i] = silu(gu[m][i]) * gu[m][I + i] for a gate_up GEMM output whose row m holds the
+ * gate half [0, I) and the up half [I, 2I) (the SwiGLU step of the tensor-parallel MLP; the
+ * reference names this elementwise cost but has no kernel for it).  fp16, I % 8 == 0. */
+int tempo_sm100_silu_mul(const void* gu, void* out, int M, int I, int ld_gu, int ld_out,
+                         void* stream);
+
 /* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
  * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the
  * current device. */
