@@ -297,6 +297,11 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    # stdout carries exactly one JSON line: library banners (e.g. NCCL's version line) go to
+    # stderr until the result is printed
+    sys.stdout.flush()
+    real_stdout = os.dup(1)
+    os.dup2(2, 1)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
@@ -522,6 +527,8 @@ def main():
         "tp_mlp": tp_rows,
         "x_cublas_median": statistics.median(p["x_cublas"] for p in per_gemm) if per_gemm and per_gemm[0]["x_cublas"] else None,
     }
+    sys.stdout.flush()
+    os.dup2(real_stdout, 1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
