@@ -87,13 +87,31 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
     h.splits = 1;
     return M <= kGemvMaxM;
   }
-  if (h.cta_group == 2) {  // pair tiles: no split-K
+  if (h.cta_group == 2) {  // pair tiles: the width by the wave model, data-parallel
+    h.bn = choose_pair_bn(M, N, sms, h.bn);
     h.splits = 1;
-    return true;
+    return h.bn != 0;
   }
   const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
   h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes, hbm);
   return find_inst(wkind, h.bn, h.swap) != nullptr;
+}
+
+// Workspace bytes a hyperform needs (0: none) and, in *zero_bytes, how many leading bytes of it
+// are arrival counters that must be zero before a launch.
+size_t hyper_ws(int M, int N, int K, const Hyper& h, int sms, size_t ws_cap, size_t* zero_bytes) {
+  if (h.cta_group == 2) {
+    const PairPlan pl = pair_plan(M, N, K, h.bn, sms, h.max_ctas, h.splits > 1, ws_cap);
+    if (zero_bytes)
+      *zero_bytes = pl.ws_bytes ? counters_used_bytes(2 * (pl.tiles - pl.sk_tile0)) : 0;
+    return pl.ws_bytes;
+  }
+  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
+  const int bn = std::max(h.bn, 1);
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + bn - 1) / bn);
+  const size_t need = h.bn == 0 ? 0 : ws_needed(tiles, h.splits, h.bn);
+  if (zero_bytes) *zero_bytes = need ? counters_used_bytes(tiles) : 0;
+  return need;
 }
 
 cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
@@ -153,10 +171,9 @@ int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, cons
 
 size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind) {
   Hyper h{};
-  if (!select_hyper(weight_kind, M, N, K, (size_t)1 << 40, h, current_sms())) return 0;
-  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
-  return ws_needed(tiles, h.splits, h.bn);
+  const int sms = current_sms();
+  if (!select_hyper(weight_kind, M, N, K, (size_t)1 << 40, h, sms)) return 0;
+  return hyper_ws(M, N, K, h, sms, (size_t)1 << 40, nullptr);
 }
 
 int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, const void* scale,
@@ -183,9 +200,9 @@ int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W,
     return tempo_sm100_gemm_hyperform(weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc,
                                       group_size, bn, swap, splits, group_m, max_ctas, ws, ws_bytes,
                                       stream);
-  if (weight_kind != 0 || swap || splits > 1) return cudaErrorInvalidConfiguration;
+  if (weight_kind != 0 || swap) return cudaErrorInvalidConfiguration;
   if (!fp16_applicable(A, W, C, M, N, K, lda, ldw, ldc)) return cudaErrorInvalidConfiguration;
-  Hyper h{bn, 0, 1, group_m < 1 ? 1 : group_m, max_ctas};
+  Hyper h{bn, 0, splits > 1 ? 2 : 1, group_m < 1 ? 1 : group_m, max_ctas};
   h.cta_group = 2;
   Problem pr{0, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
   return run(pr, h, static_cast<cudaStream_t>(stream));
@@ -312,16 +329,15 @@ extern "C" int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void*
 
   // Same choice as tempo_sm100_gemm_fp16 given a workspace of tempo_sm100_workspace_bytes.
   Hyper h{};
-  if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, current_sms()))
-    return cudaErrorInvalidConfiguration;
-  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
-  const size_t need = ws_needed(tiles, h.splits, h.bn);
+  const int sms = current_sms();
+  if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, sms)) return cudaErrorInvalidConfiguration;
+  size_t zero_bytes = 0;
+  const size_t need = hyper_ws(M, N, K, h, sms, (size_t)1 << 40, &zero_bytes);
   if (need > (size_t)TEMPO_SM100_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (need > 0) {
     // The counters must start at zero; the array keeps whatever the previous call left.
-    e = cudaMemsetAsync(scratch, 0, counters_bytes(tiles), st);
+    e = cudaMemsetAsync(scratch, 0, zero_bytes, st);
     if (e != cudaSuccess) return e;
   }
   Problem pr{0, A, B, nullptr, nullptr, C, M, N, K, lda, ldb, ldc, 0, scratch,

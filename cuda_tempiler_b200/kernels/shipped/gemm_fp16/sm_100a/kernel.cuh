@@ -448,6 +448,11 @@ struct GemmArgs {
   int groups_per_row;   // K / group_size
   int weight_rows;      // N (rows of the weight operand)
   int sz_bytes;         // group-wise: scale + zero bytes one stage loads
+  // Stream-K region of the 2-CTA kernel: tiles [sk_tile0, tiles) are cut into one contiguous
+  // run of k-blocks per cluster (sk_clusters of them); tiles before sk_tile0 are whole units.
+  int sk_tile0;         // first stream-K tile (== tiles: none)
+  int sk_clusters;      // clusters sharing the stream-K k-blocks (0: none)
+  long long sk_iters;   // k-blocks of the stream-K region: (tiles - sk_tile0) * num_kb
 };
 
 __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -1243,6 +1248,70 @@ namespace tempo_sm100 {
 // barrier; tcgen05.commit multicasts stage release and accumulator-ready to both CTAs; both
 // epilogues report accumulator-consumed to the leader.  Non-swapped, no split-K.
 // ---------------------------------------------------------------------------------------------
+// One unit of work of the 2-CTA kernel: k-blocks [kb0, kb1) of a tile.  contrib is the number
+// of clusters whose k-block runs meet in this tile (1: the cluster owns the whole tile) and
+// slot this cluster's place among them, in k order.  Partial slot of (stream-K tile t, cluster
+// c) is t + c: unique, because the clusters of tile t + 1 start where those of tile t end, and
+// a tile's slots are consecutive from slot0 = t + (its first cluster).
+struct PairSeg {
+  int tile, kb0, kb1, slot, contrib, slot0;
+};
+
+// Walks a cluster's units: first its whole data-parallel tiles (cluster, cluster + P, ...
+// below sk_tile0), then its contiguous run [begin(c), begin(c + 1)) of the stream-K region's
+// k-blocks, begin(c) = sk_iters * c / sk_clusters, cut at tile boundaries.
+struct PairSegIter {
+  int dp_next, P;
+  long long it, it_end;
+  __device__ __forceinline__ PairSegIter(const GemmArgs& a, int cluster, int nclusters)
+      : dp_next(cluster), P(nclusters), it(0), it_end(0) {
+    if (cluster < a.sk_clusters) {
+      it = a.sk_iters * cluster / a.sk_clusters;
+      it_end = a.sk_iters * (cluster + 1) / a.sk_clusters;
+    }
+  }
+  // owner of stream-K k-block i: the largest c with begin(c) <= i
+  __device__ __forceinline__ static int owner(const GemmArgs& a, long long i) {
+    return (int)(((i + 1) * a.sk_clusters - 1) / a.sk_iters);
+  }
+  __device__ __forceinline__ bool next(const GemmArgs& a, PairSeg& s) {
+    if (dp_next < a.sk_tile0) {
+      s.tile = dp_next;
+      s.kb0 = 0;
+      s.kb1 = a.num_kb;
+      s.slot = 0;
+      s.contrib = 1;
+      s.slot0 = 0;
+      dp_next += P;
+      return true;
+    }
+    if (it >= it_end) return false;
+    const int t = (int)(it / a.num_kb);
+    s.tile = a.sk_tile0 + t;
+    s.kb0 = (int)(it - (long long)t * a.num_kb);
+    s.kb1 = (int)min((long long)a.num_kb, s.kb0 + (it_end - it));
+    const long long first = (long long)t * a.num_kb;
+    const int c_first = owner(a, first);
+    const int c_last = owner(a, first + a.num_kb - 1);
+    s.contrib = c_last - c_first + 1;
+    s.slot0 = t + c_first;
+    s.slot = owner(a, it) - c_first;
+    it += s.kb1 - s.kb0;
+    return true;
+  }
+};
+
+// Raster position (tp, tq) of a tile (group_m rows of tiles at a time, for L2 reuse).
+__device__ __forceinline__ void tile_pos(const GemmArgs& a, int tile, int& tp, int& tq) {
+  const int gsz = a.group_m * a.tiles_q;
+  const int g = tile / gsz;
+  const int first = g * a.group_m;
+  const int gm = min(a.tiles_p - first, a.group_m);
+  const int r = tile - g * gsz;
+  tp = first + r % gm;
+  tq = r / gm;
+}
+
 template <int BN_>
 struct PairCfg {
   static constexpr int BM = 128, BN = BN_, BK = 64;
@@ -1255,8 +1324,11 @@ struct PairCfg {
   static constexpr int STAGES = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 8);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr int THREADS = 192;
-  static constexpr int TMEM_COLS = tmem_cols_for(2 * BN);
-  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  // accumulator buffer b starts at TMEM column b * ACC_STRIDE (a power of two)
+  static constexpr int ACC_STRIDE = BN <= 128 ? 128 : 256;
+  static constexpr int TMEM_COLS = tmem_cols_for(2 * ACC_STRIDE);
+  static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256,
+                "pair tiles are 256 x BN, BN in 128..256 step 32 (32-column epilogue chunks)");
   static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
 };
 
@@ -1274,6 +1346,7 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -1326,11 +1399,13 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int unit = cluster; unit < args.num_units; unit += nclusters) {
-        int tile, tp, tq, split, kb0, kb1;
-        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+      PairSegIter segs(args, cluster, nclusters);
+      PairSeg sg;
+      while (segs.next(args, sg)) {
+        int tp, tq;
+        tile_pos(args, sg.tile, tp, tq);
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, 11)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
           const uint32_t lead_full = mapa_shared(full_bar(stage), 0);
@@ -1366,16 +1441,17 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int lu = 0;
-      for (int unit = cluster; unit < args.num_units; unit += nclusters, ++lu) {
-        int tile, tp, tq, split, kb0, kb1;
-        decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+      PairSegIter segs(args, cluster, nclusters);
+      PairSeg sg;
+      for (; segs.next(args, sg); ++lu) {
+        const int kb0 = sg.kb0;
         const int buf = lu & 1;
         const uint32_t uphase = (lu >> 1) & 1;
         if (!mbar_wait_cluster(tempty_bar(buf), uphase ^ 1u, abort_flag, 12)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * Cfg::ACC_STRIDE;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 13)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
@@ -1402,16 +1478,80 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     uint8_t* stage_buf = epi_smem + (warp - 2) * 4096;
     int sb = 0;
     int lu = 0;
-    for (int unit = cluster; unit < args.num_units; unit += nclusters, ++lu) {
-      int tile, tp, tq, split, kb0, kb1;
-      decode_unit(args, unit, tile, tp, tq, split, kb0, kb1);
+    PairSegIter segs(args, cluster, nclusters);
+    PairSeg sg;
+    for (; segs.next(args, sg); ++lu) {
+      int tp, tq;
+      tile_pos(args, sg.tile, tp, tq);
       const int buf = lu & 1;
       const uint32_t uphase = (lu >> 1) & 1;
       if (!mbar_wait(tfull_bar(buf), uphase, abort_flag, 14)) break;
       tc_fence_after();
-      const uint32_t t_acc = t_lane + buf * BN;
+      const uint32_t t_acc = t_lane + buf * Cfg::ACC_STRIDE;
       const int q0 = tq * BN;
       const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
+      if (sg.contrib > 1) {
+        // Stream-K piece: this CTA's 128 x BN fp32 partial goes to its slot, [column][row] so
+        // the warp's stores are coalesced; the last of the tile's clusters to arrive sums the
+        // slots in k order (deterministic) and writes C.
+        const int skt = sg.tile - args.sk_tile0;
+        const long long slice = (long long)128 * BN;
+        float* part = args.ws + ((long long)(sg.slot0 + sg.slot) * 2 + rank) * slice;
+        const int row = quad * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float f[32];
+          acc_chunk<32, 1, BN>(t_acc, c, f);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(part + (c * 32 + j) * 128 + row, f[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 64) {
+          int* ctr = args.counters + skt * 2 + rank;
+          const int old = atomicAdd(ctr, 1);
+          const int last = old == sg.contrib - 1;
+          if (last) atomicExch(ctr, 0);  // ready for the next call
+          *last_flag = last;
+        }
+        named_barrier_sync(1, 128);
+        if (*last_flag) {
+          __threadfence();
+          const float* base = args.ws + ((long long)sg.slot0 * 2 + rank) * slice;
+          const int p = row0 + lane;
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            if (q0 + c0 >= args.rows_q || p >= args.rows_p) break;
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll 1
+            for (int j = 0; j < sg.contrib; ++j) {
+              const float* col = base + (long long)j * 2 * slice + c0 * 128 + row;
+              float x[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) x[i] = __ldcg(col + i * 128);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[i] += x[i];
+            }
+#pragma unroll
+            for (int i0 = 0; i0 < 32; i0 += 8) {
+              const int q = q0 + c0 + i0;
+              if (q >= args.rows_q) break;
+              uint4 w;
+              w.x = pack_half2(acc[i0 + 0], acc[i0 + 1]);
+              w.y = pack_half2(acc[i0 + 2], acc[i0 + 3]);
+              w.z = pack_half2(acc[i0 + 4], acc[i0 + 5]);
+              w.w = pack_half2(acc[i0 + 6], acc[i0 + 7]);
+              *reinterpret_cast<uint4*>(args.C + (long long)p * args.ldc + q) = w;
+            }
+          }
+        }
+        continue;
+      }
       const int live_cols = args.rows_q - q0;
       const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
       const bool rows_live = row0 < args.rows_p;

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -99,11 +100,20 @@ struct Hyper {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-size_t counters_bytes(int tiles) { return ((size_t)tiles * sizeof(int) + 255) / 256 * 256; }
+// Split workspace layout, the same for every problem: a fixed prefix of kMaxCounters arrival
+// counters, then the fp32 partials.  A fixed prefix keeps one problem's counters off another
+// problem's leftover partials when a caller reuses one workspace for different shapes; every
+// launch leaves the counters it used at zero.
+constexpr int kMaxCounters = 16384;
+constexpr size_t kCounterBytes = (size_t)kMaxCounters * sizeof(int);  // 64 KiB
+
+// Bytes of the counter prefix that n counters occupy (what must be zero before a launch).
+size_t counters_used_bytes(int n) { return ((size_t)n * sizeof(int) + 255) / 256 * 256; }
 
 size_t ws_needed(int tiles, int splits, int bn) {
   if (splits <= 1) return 0;
-  return counters_bytes(tiles) + (size_t)tiles * splits * 128 * bn * sizeof(float);
+  if (tiles > kMaxCounters) return ~(size_t)0;
+  return kCounterBytes + (size_t)tiles * splits * 128 * bn * sizeof(float);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -146,7 +156,7 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   if (a.splits > 1) {
     if (!pr.ws || pr.ws_bytes < ws_needed(tiles, a.splits, BN)) return cudaErrorInvalidValue;
     a.counters = static_cast<int*>(pr.ws);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + counters_bytes(tiles));
+    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
   }
   a.scale = static_cast<const __half*>(pr.scale);
   a.zero = static_cast<const uint8_t*>(pr.zero);
@@ -256,7 +266,49 @@ const InstEntry kInst[] = {
     TEMPO_INST_WQ(256, false),
 };
 
-// 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs.
+// Work split of the 2-CTA kernel.  P clusters (one per SM pair).  When the tiles do not fill
+// a whole number of waves, the last partial wave plus one full wave (or every tile, with fewer
+// tiles than clusters) become the stream-K region: its k-blocks are dealt out as one
+// contiguous run per cluster, so every cluster finishes at the same time and a tile is shared
+// by at most a few clusters, whose fp32 partials the last to arrive adds up.  Workspace: the
+// counter prefix (2 counters per stream-K tile), then (tiles + clusters) slots of
+// 2 x [BN][128] fp32.
+struct PairPlan {
+  int clusters = 0, tiles = 0, num_kb = 0;
+  int sk_tile0 = 0, sk_clusters = 0;
+  long long sk_iters = 0;
+  size_t ws_bytes = 0;  // workspace the stream-K region needs (0: none)
+};
+
+constexpr int kPairMinSkRun = 8;  // fewest k-blocks a cluster's stream-K run may have
+
+PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool stream_k,
+                   size_t ws_bytes) {
+  PairPlan pl;
+  pl.tiles = ((M + 255) / 256) * ((N + bn - 1) / bn);
+  pl.num_kb = (K + 63) / 64;
+  const int P = std::max(1, (max_ctas > 0 ? std::min(max_ctas, sms) : sms) / 2);
+  pl.clusters = std::min(pl.tiles, P);
+  pl.sk_tile0 = pl.tiles;
+  if (!stream_k || pl.tiles % P == 0) return pl;
+  // Worth it only if the last wave is far from full.
+  const double waves = (double)pl.tiles / P;
+  if (std::ceil(waves) - waves < 0.15) return pl;
+  const int full = pl.tiles / P;
+  const int sk_tiles = pl.tiles % P + (full >= 1 ? P : 0);
+  PairPlan sk = pl;
+  sk.clusters = P;
+  sk.sk_tile0 = pl.tiles - sk_tiles;
+  sk.sk_iters = (long long)sk_tiles * pl.num_kb;
+  sk.sk_clusters = (int)std::max(1LL, std::min<long long>(P, sk.sk_iters / kPairMinSkRun));
+  sk.ws_bytes = kCounterBytes +
+                (size_t)(sk_tiles + sk.sk_clusters) * 2 * 128 * (size_t)bn * sizeof(float);
+  if (sk.ws_bytes > ws_bytes) return pl;
+  return sk;
+}
+
+// 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs; h.splits > 1
+// enables the stream-K region of pair_plan.
 template <int BN>
 cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   using Cfg = PairCfg<BN>;
@@ -274,7 +326,9 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     });
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
   }
-  if (pr.wkind != 0 || h.swap || h.splits > 1) return cudaErrorInvalidConfiguration;
+  if (pr.wkind != 0 || h.swap) return cudaErrorInvalidConfiguration;
+  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas, h.splits > 1,
+                                pr.ws ? pr.ws_bytes : 0);
   GemmArgs a{};
   a.rows_p = pr.M;
   a.rows_q = pr.N;
@@ -288,6 +342,13 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.C = static_cast<__half*>(pr.C);
   a.ldc = pr.ldc;
   a.weight_rows = pr.N;
+  a.sk_tile0 = pl.sk_tile0;
+  a.sk_clusters = pl.sk_clusters;
+  a.sk_iters = pl.sk_iters;
+  if (pl.sk_clusters > 0) {
+    a.counters = static_cast<int*>(pr.ws);
+    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
+  }
   CUtensorMap mA, mB, mC;
   std::memset(&mA, 0, sizeof(mA));
   std::memset(&mB, 0, sizeof(mB));
@@ -297,9 +358,7 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
   ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
-  const int sms = dev_info(dev).sms;
-  const int max_clusters = std::max(1, (h.max_ctas > 0 ? h.max_ctas : sms) / 2);
-  const int clusters = std::min(a.num_units, max_clusters);
+  const int clusters = pl.clusters;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(Cfg::THREADS);
@@ -318,21 +377,59 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
 }
 
 cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  if (h.bn == 256) return launch_pair<256>(pr, h, st);
-  if (h.bn == 128) return launch_pair<128>(pr, h, st);
-  return cudaErrorInvalidConfiguration;
+  switch (h.bn) {
+    case 256: return launch_pair<256>(pr, h, st);
+    case 224: return launch_pair<224>(pr, h, st);
+    case 192: return launch_pair<192>(pr, h, st);
+    case 160: return launch_pair<160>(pr, h, st);
+    case 128: return launch_pair<128>(pr, h, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
+// Tile widths of the 2-CTA kernel, widest first.
+constexpr int kPairBn[] = {256, 224, 192, 160, 128};
+
+// The 2-CTA tile width for an M x N problem: the fewest waves of 256 x bn tiles over the
+// clusters, each wave costing bn + a fixed per-tile share (A re-read, epilogue) of 24 columns;
+// ties go to the wider tile.  bn_max caps the choice (the ladder row's bn).
+int choose_pair_bn(int M, int N, int sms, int bn_max) {
+  if (sms <= 0) return bn_max;  // no device to size waves for
+  const int P = std::max(1, sms / 2);
+  int best = 0;
+  long long best_c = 0;
+  for (int bn : kPairBn) {
+    if (bn > bn_max) continue;
+    const long long tiles = (long long)((M + 255) / 256) * ((N + bn - 1) / bn);
+    const long long c = (tiles + P - 1) / P * (bn + 24);
+    if (best == 0 || c < best_c) {
+      best = bn;
+      best_c = c;
+    }
+  }
+  return best;
+}
+
+template <int BN>
+void pair_facts(int* out6) {
+  out6[0] = PairCfg<BN>::THREADS;
+  out6[1] = PairCfg<BN>::SMEM;
+  out6[2] = PairCfg<BN>::STAGES;
+  out6[3] = PairCfg<BN>::TMEM_COLS;
 }
 
 int pair_resources(int bn, int* out6) {
-  const void* kern = bn == 256 ? reinterpret_cast<const void*>(&k_gemm_sm100_pair<256>)
-                   : bn == 128 ? reinterpret_cast<const void*>(&k_gemm_sm100_pair<128>) : nullptr;
-  if (!kern) return cudaErrorInvalidConfiguration;
+  const void* kern = nullptr;
+  switch (bn) {
+    case 256: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<256>); pair_facts<256>(out6); break;
+    case 224: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<224>); pair_facts<224>(out6); break;
+    case 192: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<192>); pair_facts<192>(out6); break;
+    case 160: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<160>); pair_facts<160>(out6); break;
+    case 128: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<128>); pair_facts<128>(out6); break;
+    default: return cudaErrorInvalidConfiguration;
+  }
   cudaFuncAttributes fa{};
   const cudaError_t err = cudaFuncGetAttributes(&fa, kern);
-  out6[0] = 192;
-  out6[1] = bn == 256 ? PairCfg<256>::SMEM : PairCfg<128>::SMEM;
-  out6[2] = bn == 256 ? PairCfg<256>::STAGES : PairCfg<128>::STAGES;
-  out6[3] = bn == 256 ? PairCfg<256>::TMEM_COLS : PairCfg<128>::TMEM_COLS;
   out6[4] = err == cudaSuccess ? fa.numRegs : -1;
   out6[5] = err == cudaSuccess ? (int)fa.localSizeBytes : -1;
   return err;

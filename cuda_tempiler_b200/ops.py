@@ -113,8 +113,12 @@ def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, spl
         out = torch.empty((M, N), dtype=torch.float16, device=A.device)
     tiles = -(-(N if swap else M) // 128) * -(-(M if swap else N) // max(bn, 1))
     nb = 0
-    if splits > 1:
-        nb = ((tiles * 4 + 255) // 256) * 256 + tiles * splits * 128 * bn * 4
+    if splits > 1 and cta_group == 2:
+        # stream-K bound: 2 counters per tile of at most 2 waves, (3 x clusters) slot pairs
+        P = torch.cuda.get_device_properties(A.device).multi_processor_count // 2
+        nb = 65536 + 3 * P * 2 * 128 * bn * 4
+    elif splits > 1:  # the fixed 64 KiB counter prefix, then the partials
+        nb = 65536 + tiles * splits * 128 * bn * 4
     ws = workspace(A.device, nb)
     rc = lib.tempo_sm100_gemm_hyperform_cg(
         kind, _ptr(A), _ptr(W), _ptr(scale), _ptr(zero), _ptr(out), M, N, K, A.stride(0),

@@ -221,9 +221,20 @@ def cmd_ship(a):
     except Exception:
         pass
     for op, kinds in (("gemm_fp16", (0,)), ("gemm_w8a16", (1, 2))):
-        lad = ship.derive_ladder(rows, kinds) if rows else list(ship.DEFAULT_LADDER)
-        measured = [{"kind": r["kind"], "name": r.get("name"), "M": r["M"], "N": r["N"], "K": r["K"],
-                     "best": r["best"], "dispatch": r["dispatch"]} for r in rows if r["kind"] in kinds]
+        prev = os.path.join(root, op, "sm_100a", "manifest.json")
+        if rows:
+            lad = ship.derive_ladder(rows, kinds)
+            measured = [{"kind": r["kind"], "name": r.get("name"), "M": r["M"], "N": r["N"],
+                         "K": r["K"], "best": r["best"], "dispatch": r["dispatch"]}
+                        for r in rows if r["kind"] in kinds]
+        elif os.path.exists(prev):  # re-freeze the skeleton under the ladder already shipped
+            m0 = json.load(open(prev))
+            lad = [(r["m_max"], r["bn"], r["swap"], r["group_m"], r.get("cta_group", 1))
+                   for r in m0["ladder"]]
+            lad[-1] = (ship.INF,) + lad[-1][1:]
+            measured = m0.get("rows", [])
+        else:
+            lad, measured = list(ship.DEFAULT_LADDER), []
         m = ship.write_ship(op, lad, root, build_facts=facts, measured=measured)
         print(f"shipped {op}: ladder {m['ladder']}")
     if facts:

@@ -11,7 +11,10 @@ an optional shared-memory dequant stage for 8-bit weights.  Axes:
   weight     0 fp16, 1 int8 per-channel (scale in the epilogue), 2 uint8 group-wise
              ((q - z) * s applied in the dequant stage, since s varies along K)
   stages     derived: the deepest ring that fits 227 KB next to the epilogue staging
-  cta_group  1 (a 2-SM pair without multicast is declared but not instantiated)
+  cta_group  1, or 2: fp16 256 x bn tiles (bn 128..256 step 32) on a 2-CTA cluster
+             (tcgen05.mma.cta_group::2), the width picked by a wave-count model, where
+             splits 2 turns a ragged last wave into a stream-K region (one contiguous k-block
+             run per cluster, partials reduced by the last cluster to finish a tile)
   tmem_bufs  2 (double-buffered fp32 accumulator)
 
 The operation contract follows the reference (C = A * B^T, layouts a=k b=k c=n, fp32
@@ -34,6 +37,7 @@ BM, BK = 128, 64
 MAX_DYN_SMEM = 232448
 SWAP_BN = (16, 32, 64, 128)
 PREFILL_BN = (64, 128, 256)
+PAIR_BN = (256, 224, 192, 160, 128)  # 2-CTA tile widths (k_gemm_sm100_pair<BN>)
 SPLITS = (1, 2, 3, 4, 6, 8)
 
 
@@ -46,8 +50,9 @@ def pair_cfg(bn: int) -> dict:
     stage = BM * BK * 2 + _ru((bn // 2) * BK * 2, 1024)
     epi, bar = 4 * 2 * 2048, 512
     stages = min((MAX_DYN_SMEM - 1024 - epi - bar) // stage, 8)
+    acc_stride = 128 if bn <= 128 else 256  # TMEM columns per accumulator buffer
     return dict(stage_bytes=stage, stages=stages, smem=1024 + stages * stage + epi + bar,
-                threads=192, tmem_cols=2 * bn)
+                threads=192, tmem_cols=2 * acc_stride)
 
 
 def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
@@ -137,9 +142,12 @@ def problem_geometry(op, p):
     M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
     rows_p, rows_q = (N, M) if p["swap"] else (M, N)
     tiles = math.ceil(rows_p / BM) * math.ceil(rows_q / p["bn"])
+    num_kb = math.ceil(K / BK)
     if p.get("cta_group", 1) == 2:
         tiles = 2 * math.ceil(M / 256) * math.ceil(N / p["bn"])
-    num_kb = math.ceil(K / BK)
+        if p["splits"] > 1:  # stream-K: the k-blocks spread evenly over the SMs
+            return dict(tiles=tiles, num_kb=num_kb, splits=1, units=tiles,
+                        kb_per_unit=num_kb, balanced=True)
     splits = max(1, min(p["splits"], num_kb))
     return dict(tiles=tiles, num_kb=num_kb, splits=splits, units=tiles * splits,
                 kb_per_unit=math.ceil(num_kb / splits))
@@ -192,12 +200,13 @@ class Sm100Skeletons:
         if M <= 256:
             forms += [(bn, 1) for bn in SWAP_BN]
         forms += [(bn, 0) for bn in PREFILL_BN]
-        if wq == 0 and M > 128:  # 2-CTA cluster tiles (cta_group::2), no split-K
-            for bn in (256, 128):
-                c = pair_cfg(bn)
-                p = dict(family=FAMILY, bn=bn, swap=0, splits=1, group_m=16, weight=0,
-                         stages=c["stages"], cta_group=2, tmem_bufs=2)
-                forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
+        if wq == 0 and M > 128:  # 2-CTA cluster tiles (cta_group::2); splits 2 = stream-K
+            for bn in PAIR_BN:
+                for splits in (1, 2):
+                    c = pair_cfg(bn)
+                    p = dict(family=FAMILY, bn=bn, swap=0, splits=splits, group_m=16, weight=0,
+                             stages=c["stages"], cta_group=2, tmem_bufs=2)
+                    forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
         for bn, swap in forms:
             for splits in SPLITS:
                 if splits > 1 and splits > num_kb // 2:
@@ -244,8 +253,12 @@ class Sm100Skeletons:
             return [Atom(0, AtomKind.MEM_READ, "LDG.128.STREAM", {"HBM": hbm}),
                     Atom(1, AtomKind.COMPUTE, "HFMA2", {"FMA": 2.0 * M * N * K / sms})]
         g = problem_geometry(op, p)
-        waves = math.ceil(g["units"] / sms)
-        kb = waves * g["kb_per_unit"]
+        if g.get("balanced"):
+            kb = g["units"] * g["kb_per_unit"] / sms
+            waves = g["units"] / sms
+        else:
+            waves = math.ceil(g["units"] / sms)
+            kb = waves * g["kb_per_unit"]
         bn, wq = p["bn"], p["weight"]
         flops = kb * 2.0 * BM * bn * BK
         b_rows = bn // 2 if p.get("cta_group", 1) == 2 else bn  # B rows this SM holds

@@ -94,9 +94,11 @@ def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=N
         cands = [(bn, sw) for bn, sw in cands
                  if bn == 0 or (sw and bn >= min(M, 128) and bn <= max(16, 2 * M))
                  or (not sw and M >= 128)]
-    pair = [(bn, 2) for bn in (256, 128)] if kind == 0 and M >= 512 else []
-    for bn, cg in pair:
-        f = lambda: ops.gemm_hyperform(p["A"], p["W"], bn=bn, swap=False, cta_group=2, group_m=16)
+    pair = [(bn, sk) for bn in (256, 224, 192, 160, 128) for sk in (1, 2)] \
+        if kind == 0 and M >= 512 else []
+    for bn, sk in pair:
+        f = lambda: ops.gemm_hyperform(p["A"], p["W"], bn=bn, swap=False, cta_group=2, group_m=16,
+                                       splits=sk)
         try:
             out = f()
         except NotCovered:
@@ -104,10 +106,10 @@ def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=N
         torch.cuda.synchronize()
         rel = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
         if not rel <= 3e-3:
-            rows.append(dict(bn=bn, swap=0, splits=1, cg=2, status="FAILGATE", rel=rel))
+            rows.append(dict(bn=bn, swap=0, splits=sk, cg=2, status="FAILGATE", rel=rel))
             continue
         t, tc = time_paired(f, cublas, flush, rounds)
-        rows.append(dict(bn=bn, swap=0, splits=1, cg=2, us=t * 1e3, cublas_us=tc * 1e3,
+        rows.append(dict(bn=bn, swap=0, splits=sk, cg=2, us=t * 1e3, cublas_us=tc * 1e3,
                          x_cublas=tc / t, rel=rel, status="CAND"))
     for bn, swap in cands:
         model = ops.select(kind, M, N, K)

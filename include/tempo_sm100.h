@@ -17,7 +17,8 @@
  *   8 (16 bytes); base pointers 16-byte aligned; K and N multiples of 8.
  *
  * Workspace: split-K launches need `ws` (device memory, zero-filled once by the caller before
- * its first use; every launch leaves it zero-filled again).  Query the size with
+ * its first use).  Its first 64 KiB hold arrival counters, which every launch leaves at zero;
+ * the rest holds fp32 partials, which need no clearing.  Query the size with
  * tempo_sm100_workspace_bytes.  ws == NULL or too small is legal: the dispatcher then picks
  * a configuration without split-K.  One workspace must not be shared by launches that can
  * run concurrently (different streams).
@@ -76,7 +77,10 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
 
 /* As tempo_sm100_gemm_hyperform with the cluster axis: cta_group 2 runs fp16 prefill tiles of
  * 256 x bn (bn 128 or 256) on 2-CTA clusters with tcgen05.mma.cta_group::2 (weight_kind 0,
- * swap 0, splits 1 only); cta_group 1 is tempo_sm100_gemm_hyperform. */
+ * swap 0).  There splits 1 = one cluster per tile; splits > 1 lets a ragged last wave run as
+ * stream-K (each cluster a contiguous run of k-blocks; needs up to
+ * 65536 + 3 * P * 2 * 128 * bn * 4 bytes of workspace for P = SMs / 2 clusters, else the
+ * launch stays data-parallel).  cta_group 1 is tempo_sm100_gemm_hyperform. */
 int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W, const void* scale,
                                   const void* zero, void* C, int M, int N, int K, int lda, int ldw,
                                   int ldc, int group_size, int bn, int swap, int splits,

@@ -101,7 +101,22 @@ def test_workspace_left_zero(dev):
     assert ops.device_status() == [0, 0, 0, 0]
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+def test_workspace_reuse_across_shapes(dev):
+    """One workspace serves split-K problems of different tile counts in a row: a 30-tile
+    problem leaves fp32 partials behind, then a 240-tile problem needs more counters than the
+    first; the counters sit in a fixed prefix, so they never land on the old partials."""
+    from cuda_tempiler_b200 import ops
+    big = lambda: _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=2,
+                                                            out=out), 16, 30720, 1024, seed=6)
+    _gate(*big())  # sizes the cached workspace for both problems
+    small = _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=3,
+                                                       out=out), 16, 3840, 4096, seed=5)
+    _gate(*small)
+    _gate(*big())
+    assert ops.device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("bn", [128, 160, 192, 224, 256])
 @pytest.mark.parametrize("M,N,K", [(260, 784, 1032), (1000, 1000, 520), (640, 768, 4096),
                                    (4096, 15360, 3840)])
 def test_pair_tiles_cta_group2(dev, bn, M, N, K):
@@ -118,9 +133,48 @@ def test_pair_resources_match_python_plan(dev):
     from cuda_tempiler_b200 import _lib
     from cuda_tempiler_b200.tempo.plugins.sm100.skeletons_py import pair_cfg
     lib = _lib.load()
-    for bn in (128, 256):
+    for bn in (128, 160, 192, 224, 256):
         out = (C.c_int * 6)()
         assert lib.tempo_sm100_pair_resources(bn, out) == 0
         c = pair_cfg(bn)
         assert (out[0], out[1], out[2], out[3]) == (c["threads"], c["smem"], c["stages"], c["tmem_cols"])
         assert out[5] == 0
+
+
+# Stream-K tails of the 2-CTA kernel: fewer tiles than clusters (every tile shared), a ragged
+# last wave (one wave + the remainder shared), few tiles with many k-blocks (a tile spread over
+# many clusters), and odd edges.
+SK_SHAPES = [(1000, 1000, 1000), (1024, 3840, 4096), (4096, 3840, 1024), (2048, 3840, 2048),
+             (520, 776, 8192), (264, 136, 4096)]
+
+
+@pytest.mark.parametrize("bn", [128, 224, 256])
+@pytest.mark.parametrize("M,N,K", SK_SHAPES)
+def test_pair_stream_k(dev, bn, M, N, K):
+    """Stream-K pair launches pass the gate, are bit-identical run to run (partials are summed
+    in k order) and leave their arrival counters at zero."""
+    from cuda_tempiler_b200 import ops
+    f = lambda A, B, out: ops.gemm_hyperform(A, B, bn=bn, swap=False, cta_group=2, splits=2,
+                                             out=out)
+    a, b, c = _run(f, M, N, K)
+    _gate(a, b, c)
+    _, _, c2 = _run(f, M, N, K)
+    assert np.array_equal(c.view(np.int16), c2.view(np.int16))
+    from test_stream_k_cpu import plan
+    pl = plan(M, N, K, bn, torch.cuda.get_device_properties(0).multi_processor_count)
+    n_ctr = 2 * (pl["tiles"] - pl["sk_tile0"])
+    ws = ops._ws_cache[(0, torch.cuda.current_stream().cuda_stream)]
+    assert int(ws[: 4 * n_ctr].view(torch.int32).abs().sum()) == 0
+    assert ops.device_status() == [0, 0, 0, 0]
+
+
+def test_dispatch_pair_width_by_waves(dev):
+    """The dispatcher's 2-CTA row narrows the tile where 256 wide leaves a ragged last wave
+    (down projection, M = 1024: 60 tiles of 256 on 74 clusters -> 72 tiles of 224), and the
+    result passes the gate."""
+    from cuda_tempiler_b200 import ops
+    sel = ops.select(0, 1024, 3840, 15360)
+    assert (sel["bn"], sel["splits"]) == (224, 1)
+    assert ops.select(0, 4096, 30720, 3840)["bn"] == 256
+    a, b, c = _run(ops.gemm_fp16, 1024, 3840, 15360, seed=3)
+    _gate(a, b, c)

@@ -70,4 +70,7 @@ def test_library_ladder_agrees_with_select_on_cpu():
         out = (C.c_int * 5)()
         assert lib.tempo_sm100_select(0, M, 4096, 4096, 0, out) == 0
         s = sel.select("gemm_fp16", M, 4096, 4096)
-        assert (out[0], out[1], out[3]) == (s["bn"], s["swap"], s["group_m"]), M
+        if s["cta_group"] == 2:  # 2-CTA width: a wave model over the SM count (none here)
+            assert out[0] >= s["bn"] and (out[1], out[3]) == (s["swap"], s["group_m"]), M
+        else:
+            assert (out[0], out[1], out[3]) == (s["bn"], s["swap"], s["group_m"]), M
