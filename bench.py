@@ -12,8 +12,11 @@ Weights N(0, 0.02), activations N(0, 1), seeded synthetic (no checkpoints).
   e2e        the same metric through the C-ABI entry point with HOST buffers: every step
              copies each GEMM's activations from pinned host memory and reads every C back.
   roofline   of the dominant kernel (largest share of the step), CUDA-event timed.
-  per_gemm   per shape x M: TFLOP/s, GB/s, bound, fraction of the measured roofline,
-             x cuBLAS (torch F.linear on the same inputs) and x naive INPUT (M <= 128).
+  per_gemm   per shape x M, each GEMM timed on its own (launches queued back to back over
+             weight copies that defeat L2): TFLOP/s, GB/s, bound, fraction of the measured
+             roofline, x cuBLAS (torch.mm timed the same way) and x naive INPUT (M <= 128);
+             in_step_us is the in-step event window.
+  x_cublas_step  cuBLAS time for the whole step (the same 20 GEMMs queued) / ours.
   cpu_baseline  fp32 numpy matmul (the reference's CPU path) on a bounded sample, rank 0.
 
 L2: every step streams 448 MB of distinct weights and consecutive GEMMs use different weight
@@ -346,9 +349,12 @@ def main():
             run_gemm(i)
     torch.cuda.synchronize()
 
-    # ---- timed region: exactly K steps, per-GEMM events inside, barrier + sync both sides
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(n)] for _ in range(min(args.steps, 50))]
+    # ---- timed region: exactly K steps, barrier + sync both sides.  Events bracket only the
+    # dominant GEMM (the most FLOPs: gate_up at M = 4096) inside the step, for the roofline;
+    # events between every pair of kernels would break their programmatic launch overlap.
+    dom = max(range(n), key=lambda i: WL.flops(gemms[i]["M"], gemms[i]["N"], gemms[i]["K"]))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -358,13 +364,12 @@ def main():
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for k in range(args.steps):
-        evk = ev[k] if k < len(ev) else None
         for i in range(n):
-            if evk:
-                evk[i][0].record(stream)
+            if i == dom:
+                ev[k][0].record(stream)
             run_gemm(i)
-            if evk:
-                evk[i][1].record(stream)
+            if i == dom:
+                ev[k][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -376,8 +381,7 @@ def main():
         ms_total = float(tt.item())
     ms_step = ms_total / args.steps
     value = flops_step * world / (ms_step * 1e-3) / 1e12
-    per_ms = [statistics.median(ev[k][i][0].elapsed_time(ev[k][i][1]) for k in range(len(ev)))
-              for i in range(n)]
+    dom_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
     status = ops.device_status(reset=True)
     if status[0] != 0:
         raise RuntimeError(f"device status {status}: a bounded wait timed out")
@@ -414,40 +418,71 @@ def main():
         e2e_ms = float(tt.item())
     e2e_value = flops_step * world / (e2e_ms * 1e-3) / 1e12
 
-    # ---- per-GEMM bars: cuBLAS (torch F.linear) and the naive INPUT kernel (M <= 128)
+    # ---- per-GEMM times and bars, each GEMM on its own: R launches queued back to back over
+    # enough weight copies that consecutive launches miss L2 (the in-step event windows above
+    # are skewed by programmatic launch overlap between neighbouring kernels).  cuBLAS
+    # (torch.mm, the same A, W copies and output) is timed the same way, and also over the
+    # whole step; the naive INPUT kernel on its own for M <= 128.
     peaks = load_peaks()
     per_gemm = []
+    own_ms = [None] * n
     cublas_ms = [None] * n
     naive_ms = [None] * n
+    cublas_step_ms = None
     if not args.no_bars:
-        def t_of(f, reps):
-            es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(reps)]
-            for a, b in es:
-                a.record(stream)
-                f()
-                b.record(stream)
-            torch.cuda.synchronize()
-            return statistics.median(a.elapsed_time(b) for a, b in es)
+        copies = {}
+        for x in gemms:
+            if x["name"] not in copies:
+                nb = x["W"].numel() * 2
+                c = min(8, max(1, -(-2 * 126 * 2**20 // nb)))
+                copies[x["name"]] = [x["W"]] + [x["W"].clone() for _ in range(c - 1)]
 
-        F = torch.nn.functional
-        for _ in range(2):
-            for x in gemms:
-                F.linear(x["A"], x["W"])
-        torch.cuda.synchronize()
-        # interleave in the same order as the timed step so L2 state matches
-        reps = 10
-        samples = [[] for _ in range(n)]
-        for _ in range(reps):
-            for i, x in enumerate(gemms):
-                samples[i].append(t_of(lambda: F.linear(x["A"], x["W"]), 1))
-        cublas_ms = [statistics.median(s) for s in samples]
+        def loop_ms(call, ws_list, reps=24):
+            for w in ws_list:
+                call(w)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for r in range(reps):
+                call(ws_list[r % len(ws_list)])
+            b.record(stream)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / reps
+
         for i, x in enumerate(gemms):
-            if x["M"] <= 128:
-                naive_ms[i] = t_of(lambda: ops.naive_gemm_fp16(x["A"], x["W"]), 2)
-    for i, x in enumerate(gemms):
+            M, N, K = x["M"], x["N"], x["K"]
+            Cb = torch.empty(M, N, dtype=torch.float16, device=dev)
+
+            def own(w, x=x):
+                rc = fn(x["A"].data_ptr(), w.data_ptr(), x["C"].data_ptr(), x["M"], x["N"],
+                        x["K"], x["K"], x["K"], x["N"], ws.data_ptr(), ws.numel(), sh)
+                if rc:
+                    raise RuntimeError(f"tempo_sm100_gemm_fp16 rc={rc}")
+
+            own_ms[i] = loop_ms(own, copies[x["name"]])
+            cublas_ms[i] = loop_ms(lambda w, x=x, Cb=Cb: torch.mm(x["A"], w.t(), out=Cb),
+                                   copies[x["name"]])
+            if M <= 128:
+                naive_ms[i] = loop_ms(lambda w, x=x: ops.naive_gemm_fp16(x["A"], w),
+                                      copies[x["name"]][:1], reps=3)
+        outs = [torch.empty(x["M"], x["N"], dtype=torch.float16, device=dev) for x in gemms]
+        cb_steps = max(3, min(args.steps, 50))
+        for _ in range(2):
+            for i, x in enumerate(gemms):
+                torch.mm(x["A"], x["W"].t(), out=outs[i])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(cb_steps):
+            for i, x in enumerate(gemms):
+                torch.mm(x["A"], x["W"].t(), out=outs[i])
+        b.record(stream)
+        torch.cuda.synchronize()
+        cublas_step_ms = a.elapsed_time(b) / cb_steps
+        del copies
+    for i, x in enumerate(gemms if not args.no_bars else []):
         M, N, K = x["M"], x["N"], x["K"]
-        t = per_ms[i] * 1e-3
+        t = own_ms[i] * 1e-3
         fl = WL.flops(M, N, K)
         by = WL.algorithmic_bytes(M, N, K)
         tflops = fl / t / 1e12
@@ -455,23 +490,23 @@ def main():
         t_floor = max(fl / (peaks["tc_sus"] * 1e12), by / (peaks["hbm"] * 1e9))
         bound = "tensor" if fl / (peaks["tc_sus"] * 1e12) >= by / (peaks["hbm"] * 1e9) else "hbm"
         per_gemm.append({
-            "gemm": x["name"], "M": M, "N": N, "K": K, "us": round(per_ms[i] * 1e3, 2),
+            "gemm": x["name"], "M": M, "N": N, "K": K, "us": round(own_ms[i] * 1e3, 2),
+            "in_step_us": round(dom_ms * 1e3, 2) if i == dom else None,
             "tflops": round(tflops, 1), "gbs": round(gbs, 0), "bound": bound,
             "roofline_frac": round(t_floor / t, 3),
-            "x_cublas": round(cublas_ms[i] / per_ms[i], 3) if cublas_ms[i] else None,
-            "x_naive": round(naive_ms[i] / per_ms[i], 1) if naive_ms[i] else None,
+            "x_cublas": round(cublas_ms[i] / own_ms[i], 3) if cublas_ms[i] else None,
+            "x_naive": round(naive_ms[i] / own_ms[i], 1) if naive_ms[i] else None,
             "cfg": ops.select(0, M, N, K, ws.numel()),
         })
 
     # ---- tensor-parallel W8A16 MLP, tp = world size (reported beside)
     tp_rows = [] if args.no_tp else tp_mlp_block(dev, world, rank, barrier)
 
-    # ---- roofline of the dominant kernel
-    dom = max(range(n), key=lambda i: per_ms[i])
+    # ---- roofline of the dominant kernel, from its in-step event windows
     x = gemms[dom]
     fl = WL.flops(x["M"], x["N"], x["K"])
     by = WL.algorithmic_bytes(x["M"], x["N"], x["K"])
-    t = per_ms[dom] * 1e-3
+    t = dom_ms * 1e-3
     traffic = load_traffic().get(f"{x['name']}_M{x['M']}")
     if fl / (peaks["tc_sus"] * 1e12) >= by / (peaks["hbm"] * 1e9):
         roof = {"bound": "tensor", "achieved": fl / t / 1e12, "peak": peaks["tc_sus"],
@@ -484,7 +519,7 @@ def main():
                 "peak_source": f"{peaks['src']} hbm_gbs"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = traffic
-    roof["share_of_step"] = per_ms[dom] / sum(per_ms)
+    roof["share_of_step"] = dom_ms / ms_step
 
     # ---- CPU baseline (rank 0, N = 1): fp32 numpy matmul on a bounded sample
     cpu = None
@@ -526,6 +561,8 @@ def main():
         "per_gemm": per_gemm,
         "tp_mlp": tp_rows,
         "x_cublas_median": statistics.median(p["x_cublas"] for p in per_gemm) if per_gemm and per_gemm[0]["x_cublas"] else None,
+        "x_cublas_step": cublas_step_ms / ms_step if cublas_step_ms else None,
+        "cublas_ms_per_step": cublas_step_ms,
     }
     sys.stdout.flush()
     os.dup2(real_stdout, 1)

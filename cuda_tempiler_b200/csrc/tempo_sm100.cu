@@ -87,9 +87,9 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
     h.splits = 1;
     return M <= kGemvMaxM;
   }
-  if (h.cta_group == 2) {  // pair tiles: the width by the wave model, data-parallel
-    h.bn = choose_pair_bn(M, N, sms, h.bn);
-    h.splits = 1;
+  if (h.cta_group == 2) {  // pair tiles: width and split tail by the wave model
+    h.bn = choose_pair_bn(M, N, K, sms, h.bn, ws_bytes);
+    h.splits = 2;
     return h.bn != 0;
   }
   const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;

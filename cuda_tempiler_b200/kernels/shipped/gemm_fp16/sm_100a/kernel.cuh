@@ -90,6 +90,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return mbar_wait_slow(bar, parity, abort_flag, where);
 }
 
+// Programmatic dependent launch.  pdl_wait blocks until the grids this one depends on have
+// completed and their writes are visible (immediately true when the launch did not ask for
+// programmatic serialisation); pdl_launch_dependents lets the next such grid be scheduled once
+// every CTA of this grid has started, so its launch and prologue overlap this grid's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -448,11 +457,11 @@ struct GemmArgs {
   int groups_per_row;   // K / group_size
   int weight_rows;      // N (rows of the weight operand)
   int sz_bytes;         // group-wise: scale + zero bytes one stage loads
-  // Stream-K region of the 2-CTA kernel: tiles [sk_tile0, tiles) are cut into one contiguous
-  // run of k-blocks per cluster (sk_clusters of them); tiles before sk_tile0 are whole units.
-  int sk_tile0;         // first stream-K tile (== tiles: none)
-  int sk_clusters;      // clusters sharing the stream-K k-blocks (0: none)
-  long long sk_iters;   // k-blocks of the stream-K region: (tiles - sk_tile0) * num_kb
+  // Split tail of the 2-CTA kernel: tiles [sk_tile0, sk_tile0 + sk_tiles) each run as sk_splits
+  // k-slices; tiles before sk_tile0 are whole units (sk_splits 0: no tail).
+  int sk_tile0;         // first tail tile
+  int sk_tiles;         // tail tiles
+  int sk_splits;        // k-slices per tail tile
 };
 
 __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -643,6 +652,9 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Nothing above touches global memory another grid may write: overlap it with that grid.
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -1149,6 +1161,8 @@ __global__ void __launch_bounds__(256)
   const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int n0 = warp_g * R;
   if (n0 >= N) return;
+  pdl_wait();
+  pdl_launch_dependents();
   const int nchunks = K / KC;           // K % KC == 0 (checked by applicability)
   float acc[MM][R];
 #pragma unroll
@@ -1249,31 +1263,20 @@ namespace tempo_sm100 {
 // epilogues report accumulator-consumed to the leader.  Non-swapped, no split-K.
 // ---------------------------------------------------------------------------------------------
 // One unit of work of the 2-CTA kernel: k-blocks [kb0, kb1) of a tile.  contrib is the number
-// of clusters whose k-block runs meet in this tile (1: the cluster owns the whole tile) and
-// slot this cluster's place among them, in k order.  Partial slot of (stream-K tile t, cluster
-// c) is t + c: unique, because the clusters of tile t + 1 start where those of tile t end, and
-// a tile's slots are consecutive from slot0 = t + (its first cluster).
+// of k-slices the tile is cut into (1: the cluster owns the whole tile), slot this unit's
+// k-slice and t the tile's place in the tail.
 struct PairSeg {
-  int tile, kb0, kb1, slot, contrib, slot0;
+  int tile, kb0, kb1, slot, contrib, t;
 };
 
-// Walks a cluster's units: first its whole data-parallel tiles (cluster, cluster + P, ...
-// below sk_tile0), then its contiguous run [begin(c), begin(c + 1)) of the stream-K region's
-// k-blocks, begin(c) = sk_iters * c / sk_clusters, cut at tile boundaries.
+// Walks a cluster's units: its whole tiles (cluster, cluster + P, ... below sk_tile0), then
+// its tail units u = cluster, cluster + P, ... below sk_tiles * sk_splits, numbered k-slice
+// major (u = slice * sk_tiles + t) so that the clusters of one wave work on neighbouring
+// k-slices and the tail's operand panels stay in L2.
 struct PairSegIter {
-  int dp_next, P;
-  long long it, it_end;
+  int dp_next, u, P;
   __device__ __forceinline__ PairSegIter(const GemmArgs& a, int cluster, int nclusters)
-      : dp_next(cluster), P(nclusters), it(0), it_end(0) {
-    if (cluster < a.sk_clusters) {
-      it = a.sk_iters * cluster / a.sk_clusters;
-      it_end = a.sk_iters * (cluster + 1) / a.sk_clusters;
-    }
-  }
-  // owner of stream-K k-block i: the largest c with begin(c) <= i
-  __device__ __forceinline__ static int owner(const GemmArgs& a, long long i) {
-    return (int)(((i + 1) * a.sk_clusters - 1) / a.sk_iters);
-  }
+      : dp_next(cluster), u(cluster), P(nclusters) {}
   __device__ __forceinline__ bool next(const GemmArgs& a, PairSeg& s) {
     if (dp_next < a.sk_tile0) {
       s.tile = dp_next;
@@ -1281,22 +1284,19 @@ struct PairSegIter {
       s.kb1 = a.num_kb;
       s.slot = 0;
       s.contrib = 1;
-      s.slot0 = 0;
+      s.t = 0;
       dp_next += P;
       return true;
     }
-    if (it >= it_end) return false;
-    const int t = (int)(it / a.num_kb);
-    s.tile = a.sk_tile0 + t;
-    s.kb0 = (int)(it - (long long)t * a.num_kb);
-    s.kb1 = (int)min((long long)a.num_kb, s.kb0 + (it_end - it));
-    const long long first = (long long)t * a.num_kb;
-    const int c_first = owner(a, first);
-    const int c_last = owner(a, first + a.num_kb - 1);
-    s.contrib = c_last - c_first + 1;
-    s.slot0 = t + c_first;
-    s.slot = owner(a, it) - c_first;
-    it += s.kb1 - s.kb0;
+    if (a.sk_splits == 0 || u >= a.sk_tiles * a.sk_splits) return false;
+    const int slice = u / a.sk_tiles;
+    s.t = u - slice * a.sk_tiles;
+    s.tile = a.sk_tile0 + s.t;
+    s.kb0 = (int)((long long)a.num_kb * slice / a.sk_splits);
+    s.kb1 = (int)((long long)a.num_kb * (slice + 1) / a.sk_splits);
+    s.slot = slice;
+    s.contrib = a.sk_splits;
+    u += P;
     return true;
   }
 };
@@ -1391,6 +1391,9 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised before any cross-CTA traffic
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Nothing above touches global memory another grid may write: overlap it with that grid.
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (both)
@@ -1491,23 +1494,25 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       const int q0 = tq * BN;
       const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
       if (sg.contrib > 1) {
-        // Stream-K piece: this CTA's 128 x BN fp32 partial goes to its slot, [column][row] so
-        // the warp's stores are coalesced; the last of the tile's clusters to arrive sums the
-        // slots in k order (deterministic) and writes C.
-        const int skt = sg.tile - args.sk_tile0;
+        // Tail k-slice: this CTA's 128 x BN fp32 partial goes to slot (slice, t), laid out
+        // [32-column chunk][row][32] so each thread writes and reads its row's 128 contiguous
+        // bytes per chunk as float4s.  The last of the tile's k-slices to arrive keeps its own
+        // accumulator in TMEM, adds the other slots in k order (deterministic) and writes C.
+        const int skt = sg.t;
         const long long slice = (long long)128 * BN;
-        float* part = args.ws + ((long long)(sg.slot0 + sg.slot) * 2 + rank) * slice;
+        const long long slot_stride = 2LL * args.sk_tiles * slice;  // next k-slice, same tile
+        const float* base = args.ws + ((long long)skt * 2 + rank) * slice;
         const int row = quad * 32 + lane;
+        float4* part = reinterpret_cast<float4*>(const_cast<float*>(base) + sg.slot * slot_stride);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float f[32];
           acc_chunk<32, 1, BN>(t_acc, c, f);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) __stcg(part + (c * 32 + j) * 128 + row, f[j]);
+          for (int q = 0; q < 8; ++q)
+            __stcg(part + (c * 128 + row) * 8 + q,
+                   make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]));
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
         __threadfence();
         named_barrier_sync(1, 128);
         if (threadIdx.x == 64) {
@@ -1518,36 +1523,71 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
           *last_flag = last;
         }
         named_barrier_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          const float* base = args.ws + ((long long)sg.slot0 * 2 + rank) * slice;
-          const int p = row0 + lane;
+        const bool last = *last_flag != 0;
+        if (!last) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+          continue;
+        }
+        __threadfence();
+        const int p = row0 + lane;
+        const int S = sg.contrib;
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 32) {
-            if (q0 + c0 >= args.rows_q || p >= args.rows_p) break;
-            float acc[32];
+        for (int c = 0; c < BN / 32; ++c) {
+          float acc[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-#pragma unroll 1
-            for (int j = 0; j < sg.contrib; ++j) {
-              const float* col = base + (long long)j * 2 * slice + c0 * 128 + row;
-              float x[32];
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          // slots in k order, four at a time (32 float4 loads in flight per thread); this
+          // CTA's own slot comes from TMEM
+          for (int j0 = 0; j0 < S; j0 += 4) {
+            float4 x[4][8];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) x[i] = __ldcg(col + i * 128);
+            for (int jj = 0; jj < 4; ++jj) {
+              const int j = j0 + jj;
+              if (j < S && j != sg.slot) {
+                const float4* src = reinterpret_cast<const float4*>(base + j * slot_stride) +
+                                    (c * 128 + row) * 8;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) acc[i] += x[i];
+                for (int q = 0; q < 8; ++q) x[jj][q] = __ldcg(src + q);
+              }
             }
 #pragma unroll
-            for (int i0 = 0; i0 < 32; i0 += 8) {
-              const int q = q0 + c0 + i0;
-              if (q >= args.rows_q) break;
-              uint4 w;
-              w.x = pack_half2(acc[i0 + 0], acc[i0 + 1]);
-              w.y = pack_half2(acc[i0 + 2], acc[i0 + 3]);
-              w.z = pack_half2(acc[i0 + 4], acc[i0 + 5]);
-              w.w = pack_half2(acc[i0 + 6], acc[i0 + 7]);
-              *reinterpret_cast<uint4*>(args.C + (long long)p * args.ldc + q) = w;
+            for (int jj = 0; jj < 4; ++jj) {
+              const int j = j0 + jj;
+              if (j >= S) break;
+              if (j == sg.slot) {
+                float f[32];
+                acc_chunk<32, 1, BN>(t_acc, c, f);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] += f[i];
+              } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  acc[4 * q] += x[jj][q].x;
+                  acc[4 * q + 1] += x[jj][q].y;
+                  acc[4 * q + 2] += x[jj][q].z;
+                  acc[4 * q + 3] += x[jj][q].w;
+                }
+              }
             }
+          }
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+          }
+          if (p >= args.rows_p) continue;
+#pragma unroll
+          for (int i0 = 0; i0 < 32; i0 += 8) {
+            const int q = q0 + c * 32 + i0;
+            if (q >= args.rows_q) break;
+            uint4 w;
+            w.x = pack_half2(acc[i0 + 0], acc[i0 + 1]);
+            w.y = pack_half2(acc[i0 + 2], acc[i0 + 3]);
+            w.z = pack_half2(acc[i0 + 4], acc[i0 + 5]);
+            w.w = pack_half2(acc[i0 + 6], acc[i0 + 7]);
+            *reinterpret_cast<uint4*>(args.C + (long long)p * args.ldc + q) = w;
           }
         }
         continue;

@@ -11,7 +11,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 #include <mutex>
 
 #include "kernel.cuh"
@@ -49,18 +51,99 @@ EncodeTiledFn encode_fn() {
 }
 
 // 2-D row-major tensor [outer][inner] with row stride `ld` elements; box [box_outer][box_inner].
+// Encoding a descriptor costs about a microsecond of host time, several per launch, so the
+// descriptors of recent calls are kept in a small per-thread cache keyed by every argument (a
+// descriptor holds only the address and the geometry, so a hit is exact whatever the memory
+// holds now).
+struct MapKey {
+  const void* ptr;
+  uint64_t inner, outer, ld;
+  uint32_t box_inner, box_outer;
+  int dt, esize, sw;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && inner == o.inner && outer == o.outer && ld == o.ld &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dt == o.dt &&
+           esize == o.esize && sw == o.sw;
+  }
+};
+
+struct MapSlot {
+  MapKey key;
+  CUtensorMap map;
+  bool used = false;
+};
+
+constexpr int kMapCacheSlots = 256;
+
 bool make_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int esize, uint64_t inner,
               uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
               CUtensorMapSwizzle sw) {
+  const MapKey key{ptr, inner, outer, ld, box_inner, box_outer, (int)dt, esize, (int)sw};
+  uint64_t h = reinterpret_cast<uintptr_t>(ptr) * 0x9E3779B97F4A7C15ull;
+  for (uint64_t v : {inner, outer, ld, (uint64_t)box_inner << 32 | box_outer,
+                     (uint64_t)dt << 40 | (uint64_t)esize << 20 | (uint64_t)sw})
+    h = (h ^ v) * 0x100000001B3ull;
+  thread_local MapSlot cache[kMapCacheSlots];
+  MapSlot& slot = cache[(h >> 24) % kMapCacheSlots];
+  if (slot.used && slot.key == key) {
+    *m = slot.map;
+    return true;
+  }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {ld * (uint64_t)esize};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  slot.key = key;
+  slot.map = *m;
+  slot.used = true;
+  return true;
+}
+
+// Launch attributes every product kernel gets: programmatic dependent launch (the kernel
+// waits for its predecessors in the stream with griddepcontrol.wait after a prologue that
+// touches no shared global memory), and a cluster shape when cluster_x > 1.  Setting
+// TEMPO_SM100_PDL=0 in the environment turns programmatic launch off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TEMPO_SM100_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t st, int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 struct DevInfo {
@@ -205,8 +288,8 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   const int sms = dev_info(dev).sms;
   int grid = std::min(a.num_units, h.max_ctas > 0 ? h.max_ctas : sms);
   if (grid <= 0) return cudaErrorInvalidConfiguration;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mP, mQ, mW, mC, mS, mZ, a);
-  return cudaGetLastError();
+  return launch_ex(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM, st, 1, mP, mQ, mW, mC, mS,
+                   mZ, a);
 }
 
 // Decode-sized streaming GEMV (hyperform bn == 0): M <= 4, 256 threads, R weight rows per warp.
@@ -214,12 +297,11 @@ template <int WQ, int MM, int R>
 cudaError_t launch_gemv(const Problem& pr, cudaStream_t st) {
   const int rows_per_block = 8 * R;
   const int grid = (pr.N + rows_per_block - 1) / rows_per_block;
-  k_gemv_sm100<WQ, MM, R><<<grid, 256, 0, st>>>(
-      static_cast<const __half*>(pr.A), static_cast<const uint8_t*>(pr.W),
-      static_cast<const __half*>(pr.scale), static_cast<const uint8_t*>(pr.zero),
-      static_cast<__half*>(pr.C), pr.M, pr.N, pr.K, pr.lda, pr.ldw, pr.ldc,
-      pr.group > 0 ? pr.group : 1);
-  return cudaGetLastError();
+  return launch_ex(k_gemv_sm100<WQ, MM, R>, dim3(grid), dim3(256), 0, st, 1,
+                   static_cast<const __half*>(pr.A), static_cast<const uint8_t*>(pr.W),
+                   static_cast<const __half*>(pr.scale), static_cast<const uint8_t*>(pr.zero),
+                   static_cast<__half*>(pr.C), pr.M, pr.N, pr.K, (long long)pr.lda,
+                   (long long)pr.ldw, (long long)pr.ldc, pr.group > 0 ? pr.group : 1);
 }
 
 template <int WQ, int R>
@@ -266,23 +348,24 @@ const InstEntry kInst[] = {
     TEMPO_INST_WQ(256, false),
 };
 
-// Work split of the 2-CTA kernel.  P clusters (one per SM pair).  When the tiles do not fill
-// a whole number of waves, the last partial wave plus one full wave (or every tile, with fewer
-// tiles than clusters) become the stream-K region: its k-blocks are dealt out as one
-// contiguous run per cluster, so every cluster finishes at the same time and a tile is shared
-// by at most a few clusters, whose fp32 partials the last to arrive adds up.  Workspace: the
-// counter prefix (2 counters per stream-K tile), then (tiles + clusters) slots of
+// Work split of the 2-CTA kernel.  P clusters (one per SM pair) take whole 256 x BN tiles in
+// turn.  When the tiles leave a ragged last wave, the tiles of that wave (or every tile, with
+// fewer tiles than two waves) can instead run as a split tail: each cut into S k-slices, the
+// slices numbered k-slice major so concurrent clusters read neighbouring k ranges, and the
+// tile's last slice to finish adds the fp32 partials up in k order.  Cost in tile times:
+// whole waves + ceil(R * S / P) / S + S x (a slice's fixup against the tile's MMA cycles); the
+// tail is taken when it saves at least 3 %.  Workspace: the counter prefix (2 per tail tile), then R * S slots of
 // 2 x [BN][128] fp32.
 struct PairPlan {
   int clusters = 0, tiles = 0, num_kb = 0;
-  int sk_tile0 = 0, sk_clusters = 0;
-  long long sk_iters = 0;
-  size_t ws_bytes = 0;  // workspace the stream-K region needs (0: none)
+  int sk_tile0 = 0, sk_tiles = 0, sk_splits = 0;
+  size_t ws_bytes = 0;  // workspace the tail needs (0: none)
+  double cost = 0;      // modelled time in tile times
 };
 
-constexpr int kPairMinSkRun = 8;  // fewest k-blocks a cluster's stream-K run may have
+constexpr int kPairMinSlice = 4;  // fewest k-blocks in one tail k-slice
 
-PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool stream_k,
+PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool split_tail,
                    size_t ws_bytes) {
   PairPlan pl;
   pl.tiles = ((M + 255) / 256) * ((N + bn - 1) / bn);
@@ -290,25 +373,36 @@ PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool stre
   const int P = std::max(1, (max_ctas > 0 ? std::min(max_ctas, sms) : sms) / 2);
   pl.clusters = std::min(pl.tiles, P);
   pl.sk_tile0 = pl.tiles;
-  if (!stream_k || pl.tiles % P == 0) return pl;
-  // Worth it only if the last wave is far from full.
-  const double waves = (double)pl.tiles / P;
-  if (std::ceil(waves) - waves < 0.15) return pl;
-  const int full = pl.tiles / P;
-  const int sk_tiles = pl.tiles % P + (full >= 1 ? P : 0);
-  PairPlan sk = pl;
-  sk.clusters = P;
-  sk.sk_tile0 = pl.tiles - sk_tiles;
-  sk.sk_iters = (long long)sk_tiles * pl.num_kb;
-  sk.sk_clusters = (int)std::max(1LL, std::min<long long>(P, sk.sk_iters / kPairMinSkRun));
-  sk.ws_bytes = kCounterBytes +
-                (size_t)(sk_tiles + sk.sk_clusters) * 2 * 128 * (size_t)bn * sizeof(float);
-  if (sk.ws_bytes > ws_bytes) return pl;
-  return sk;
+  pl.cost = (double)((pl.tiles + P - 1) / P);
+  if (!split_tail || pl.tiles % P == 0) return pl;
+  const int R = pl.tiles >= P ? pl.tiles % P : pl.tiles;
+  const int full = (pl.tiles - R) / P;
+  // a k-slice's partial write and read-back: ~4000 cycles against a tile's 2 * bn per k-block
+  const double fix = 4000.0 / (pl.num_kb * 2.0 * bn);
+  double best = pl.cost * 0.97;
+  int best_s = 0;
+  // at most 3 P tail units: 3 waves of slices, and (at bn 256) under 58 MB of partials
+  for (int S = 2; S <= 16 && S * kPairMinSlice <= pl.num_kb && R * S <= 3 * P; ++S) {
+    const size_t need = kCounterBytes + (size_t)R * S * 2 * 128 * (size_t)bn * sizeof(float);
+    if (need > ws_bytes) break;
+    const double c = full + (double)((R * S + P - 1) / P) / S + S * fix;
+    if (c < best) {
+      best = c;
+      best_s = S;
+    }
+  }
+  if (best_s == 0) return pl;
+  pl.clusters = P;
+  pl.sk_tile0 = pl.tiles - R;
+  pl.sk_tiles = R;
+  pl.sk_splits = best_s;
+  pl.ws_bytes = kCounterBytes + (size_t)R * best_s * 2 * 128 * (size_t)bn * sizeof(float);
+  pl.cost = best;
+  return pl;
 }
 
 // 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs; h.splits > 1
-// enables the stream-K region of pair_plan.
+// allows the split tail of pair_plan.
 template <int BN>
 cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   using Cfg = PairCfg<BN>;
@@ -343,9 +437,9 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.ldc = pr.ldc;
   a.weight_rows = pr.N;
   a.sk_tile0 = pl.sk_tile0;
-  a.sk_clusters = pl.sk_clusters;
-  a.sk_iters = pl.sk_iters;
-  if (pl.sk_clusters > 0) {
+  a.sk_tiles = pl.sk_tiles;
+  a.sk_splits = pl.sk_splits;
+  if (pl.sk_splits > 0) {
     a.counters = static_cast<int*>(pr.ws);
     a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
   }
@@ -358,22 +452,8 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
   ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
-  const int clusters = pl.clusters;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(Cfg::THREADS);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, mA, mB, mC, a);
-  if (e != cudaSuccess) return e;
-  return cudaGetLastError();
+  return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mB, mC,
+                   a);
 }
 
 cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
@@ -387,21 +467,24 @@ cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   }
 }
 
-// Tile widths of the 2-CTA kernel, widest first.
+// Tile widths of the 2-CTA kernel, widest first, and their measured throughput per FLOP
+// relative to 256 (narrower tiles read more operand bytes per FLOP from L2; gate_up M = 4096 on
+// B200: 224 -> 0.92, 192 -> 0.82, 160 -> 0.67, 128 -> 0.55).
 constexpr int kPairBn[] = {256, 224, 192, 160, 128};
+constexpr double kPairEff[] = {1.0, 0.92, 0.82, 0.67, 0.55};
 
-// The 2-CTA tile width for an M x N problem: the fewest waves of 256 x bn tiles over the
-// clusters, each wave costing bn + a fixed per-tile share (A re-read, epilogue) of 24 columns;
-// ties go to the wider tile.  bn_max caps the choice (the ladder row's bn).
-int choose_pair_bn(int M, int N, int sms, int bn_max) {
+// The 2-CTA tile width for an M x N x K problem: the smallest modelled time, pair_plan's cost
+// (whole waves, or waves plus a split tail that fits ws_bytes) times bn / 256 / efficiency.
+// bn_max caps the choice (the ladder row's bn).
+int choose_pair_bn(int M, int N, int K, int sms, int bn_max, size_t ws_bytes) {
   if (sms <= 0) return bn_max;  // no device to size waves for
-  const int P = std::max(1, sms / 2);
   int best = 0;
-  long long best_c = 0;
-  for (int bn : kPairBn) {
+  double best_c = 0;
+  for (int i = 0; i < 5; ++i) {
+    const int bn = kPairBn[i];
     if (bn > bn_max) continue;
-    const long long tiles = (long long)((M + 255) / 256) * ((N + bn - 1) / bn);
-    const long long c = (tiles + P - 1) / P * (bn + 24);
+    const PairPlan pl = pair_plan(M, N, K, bn, sms, 0, true, ws_bytes);
+    const double c = pl.cost * bn / 256.0 / kPairEff[i];
     if (best == 0 || c < best_c) {
       best = bn;
       best_c = c;

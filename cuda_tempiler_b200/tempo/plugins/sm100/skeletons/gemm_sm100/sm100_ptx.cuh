@@ -88,6 +88,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return mbar_wait_slow(bar, parity, abort_flag, where);
 }
 
+// Programmatic dependent launch.  pdl_wait blocks until the grids this one depends on have
+// completed and their writes are visible (immediately true when the launch did not ask for
+// programmatic serialisation); pdl_launch_dependents lets the next such grid be scheduled once
+// every CTA of this grid has started, so its launch and prologue overlap this grid's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

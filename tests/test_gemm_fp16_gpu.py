@@ -141,18 +141,17 @@ def test_pair_resources_match_python_plan(dev):
         assert out[5] == 0
 
 
-# Stream-K tails of the 2-CTA kernel: fewer tiles than clusters (every tile shared), a ragged
-# last wave (one wave + the remainder shared), few tiles with many k-blocks (a tile spread over
-# many clusters), and odd edges.
-SK_SHAPES = [(1000, 1000, 1000), (1024, 3840, 4096), (4096, 3840, 1024), (2048, 3840, 2048),
+# Split tails of the 2-CTA kernel: fewer tiles than clusters (every tile cut), a ragged last
+# wave (the remainder cut), few tiles with many k-blocks (many k-slices), and odd edges.
+SK_SHAPES = [(1000, 1000, 1000), (512, 3840, 4096), (4096, 3840, 1024), (2048, 3840, 2048),
              (520, 776, 8192), (264, 136, 4096)]
 
 
 @pytest.mark.parametrize("bn", [128, 224, 256])
 @pytest.mark.parametrize("M,N,K", SK_SHAPES)
-def test_pair_stream_k(dev, bn, M, N, K):
-    """Stream-K pair launches pass the gate, are bit-identical run to run (partials are summed
-    in k order) and leave their arrival counters at zero."""
+def test_pair_split_tail(dev, bn, M, N, K):
+    """Pair launches with a split tail pass the gate, are bit-identical run to run (partials
+    are summed in k order) and leave their arrival counters at zero."""
     from cuda_tempiler_b200 import ops
     f = lambda A, B, out: ops.gemm_hyperform(A, B, bn=bn, swap=False, cta_group=2, splits=2,
                                              out=out)
@@ -162,7 +161,7 @@ def test_pair_stream_k(dev, bn, M, N, K):
     assert np.array_equal(c.view(np.int16), c2.view(np.int16))
     from test_stream_k_cpu import plan
     pl = plan(M, N, K, bn, torch.cuda.get_device_properties(0).multi_processor_count)
-    n_ctr = 2 * (pl["tiles"] - pl["sk_tile0"])
+    n_ctr = 2 * pl["sk_tiles"]
     ws = ops._ws_cache[(0, torch.cuda.current_stream().cuda_stream)]
     assert int(ws[: 4 * n_ctr].view(torch.int32).abs().sum()) == 0
     assert ops.device_status() == [0, 0, 0, 0]
@@ -174,7 +173,7 @@ def test_dispatch_pair_width_by_waves(dev):
     result passes the gate."""
     from cuda_tempiler_b200 import ops
     sel = ops.select(0, 1024, 3840, 15360)
-    assert (sel["bn"], sel["splits"]) == (224, 1)
+    assert sel["bn"] == 224
     assert ops.select(0, 4096, 30720, 3840)["bn"] == 256
     a, b, c = _run(ops.gemm_fp16, 1024, 3840, 15360, seed=3)
     _gate(a, b, c)
