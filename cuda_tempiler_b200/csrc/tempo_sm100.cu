@@ -45,25 +45,37 @@ const LadderRow* ladder_row(int wkind, int M) {
 //             and re-reads a 128xBN fp32 slice (charged 3x for the counter/barrier).
 //   HBM side: compulsory bytes (2MK + w_b NK + 2MN) at ~3400 B/cycle for the whole GPU.
 //   launch:   the larger of the two.
-double launch_cycles(int tiles, int num_kb, int sms, int bn, int s, double hbm_bytes) {
+// Cycle model of one launch (the busiest SM): waves of units, each k-block costing the larger
+// of its UMMAs and its operand feed -- weight bytes stream from HBM at about 32 B/cycle per SM
+// (measured TMA streaming rate), activation bytes from L2 at about 100 -- plus the k-split
+// fixup: ~1500 cycles through distributed shared memory (splits <= kMaxClusterSplit), the
+// fp32 partial round trip through global memory beyond; never below the HBM time.
+double launch_cycles(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, int s,
+                     double hbm_bytes) {
   const long long units = (long long)tiles * s;
   const long long waves = (units + sms - 1) / sms;
   const double mma = 4.0 * std::max(bn / 2.0, (128.0 + bn) / 4.0);
-  const double feed = (128.0 + bn) * 128.0 / 100.0;
+  const double w_rows = swap ? 128.0 : bn, a_rows = swap ? bn : 128.0;
+  const double feed = w_rows * 64.0 * wbytes / 32.0 + a_rows * 128.0 / 100.0;
   const double kb = (double)((num_kb + s - 1) / s);
-  const double fixup = s > 1 ? 3.0 * 128.0 * bn * 4.0 / 100.0 + 1500.0 : 0.0;
+  const double fixup = s == 1 ? 0.0
+                     : s <= kMaxClusterSplit ? 1500.0
+                                             : 3.0 * 128.0 * bn * 4.0 / 100.0 + 1500.0;
   const double sm_side = (double)waves * (kb * std::max(mma, feed) + fixup);
   return std::max(sm_side, hbm_bytes / 3400.0);
 }
 
-int choose_splits(int tiles, int num_kb, int sms, int bn, size_t ws_bytes, double hbm_bytes) {
+int choose_splits(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, size_t ws_bytes,
+                  double hbm_bytes) {
   if (sms <= 0) return 1;
   int best = 1;
-  double best_c = launch_cycles(tiles, num_kb, sms, bn, 1, hbm_bytes);
+  double best_c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, 1, hbm_bytes);
   const int smax = std::min(32, num_kb / 2);
   for (int s = 2; s <= smax; ++s) {
     if (ws_needed(tiles, s, bn) > ws_bytes) break;
-    const double c = launch_cycles(tiles, num_kb, sms, bn, s, hbm_bytes);
+    // a cluster k-split launch is one CTA per unit, not persistent: one wave only
+    if (s <= kMaxClusterSplit && (long long)tiles * s > sms) continue;
+    const double c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, s, hbm_bytes);
     if (c < best_c * 0.97) {
       best = s;
       best_c = c;
@@ -93,7 +105,7 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
     return h.bn != 0;
   }
   const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
-  h.splits = choose_splits(tiles, num_kb, sms, h.bn, ws_bytes, hbm);
+  h.splits = choose_splits(tiles, num_kb, sms, h.bn, h.swap, wkind == 0 ? 2 : 1, ws_bytes, hbm);
   return find_inst(wkind, h.bn, h.swap) != nullptr;
 }
 

@@ -324,6 +324,21 @@ __device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 
+// Stores into the shared memory of a CTA of this cluster (shared::cluster address).
+__device__ __forceinline__ void st_dsmem_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_dsmem_f4(uint32_t cluster_addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
 // Arrive on an mbarrier that may live in the peer CTA (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
@@ -457,6 +472,9 @@ struct GemmArgs {
   int groups_per_row;   // K / group_size
   int weight_rows;      // N (rows of the weight operand)
   int sz_bytes;         // group-wise: scale + zero bytes one stage loads
+  // k-split inside a cluster (1-CTA kernel): the cluster_split CTAs of a cluster hold the
+  // k-slices of one tile and reduce through distributed shared memory (0: not used)
+  int cluster_split;
   // Split tail of the 2-CTA kernel: tiles [sk_tile0, sk_tile0 + sk_tiles) each run as sk_splits
   // k-slices; tiles before sk_tile0 are whole units (sk_splits 0: no tail).
   int sk_tile0;         // first tail tile
@@ -465,6 +483,8 @@ struct GemmArgs {
 };
 
 __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+constexpr int kMaxClusterSplitDev = 8;  // largest k-split reduced inside one cluster
 __host__ __device__ constexpr int cmin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ constexpr int tmem_cols_for(int c) {
   return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512;
@@ -525,8 +545,15 @@ struct SkelCfg {
   // barriers: full[STAGES], empty[STAGES], deq[NDEQ] (indexed by stage, or by A slot for TA),
   // tmem full[2], tmem empty[2], done, aempty[ASLOTS]
   static constexpr int NDEQ = STAGES > ASLOTS ? STAGES : ASLOTS;
-  static constexpr int NBARS = 2 * STAGES + NDEQ + 5 + ASLOTS;
+  // + 2 for the cluster k-split: operand rings idle, partial rows delivered
+  static constexpr int NBARS = 2 * STAGES + NDEQ + 5 + ASLOTS + 2;
   static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
+  // cluster k-split: an owner's S slots of partial rows in its idle operand ring, rows of C's
+  // contiguous dimension ([q][p] swapped, [p][q] otherwise) padded by 4 floats; at most
+  // (rows + S) rows in all
+  static constexpr int PART_ROW = (SWAP ? BM : BN) + 4;
+  static_assert(((SWAP ? BN : BM) + kMaxClusterSplitDev) * PART_ROW * 4 <= STAGES * STAGE_BYTES,
+                "operand ring too small for the cluster k-split partial");
 };
 
 __device__ __forceinline__ void decode_unit(const GemmArgs& a, int unit, int& tile, int& tp,
@@ -610,6 +637,9 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   const uint32_t done_bar = bar_base + 8u * (kT0 + 4);
   // TA: aempty_bar(a) = A slot a consumed by the MMAs
   auto aempty_bar = [&](int a) { return bar_base + 8u * (kT0 + 5 + a); };
+  // cluster k-split: every CTA's operand ring idle / every CTA's partial rows delivered
+  const uint32_t rfree_bar = bar_base + 8u * (kT0 + 5 + Cfg::ASLOTS);
+  const uint32_t pready_bar = rfree_bar + 8u;
   auto p_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::P_OFF; };
   auto q_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::Q_OFF; };
   auto raw_ptr = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_OFF; };
@@ -630,6 +660,9 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     }
     mbar_init(done_bar, 1);
     for (int a = 0; a < Cfg::ASLOTS; ++a) mbar_init(aempty_bar(a), 1);
+    const int csplit = args.cluster_split > 1 ? args.cluster_split : 1;
+    mbar_init(rfree_bar, 4 * csplit);  // 4 epilogue warps of each CTA of the cluster
+    mbar_init(pready_bar, 4 * csplit);
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -650,6 +683,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (args.cluster_split > 1) cluster_sync();  // peers' barriers initialised before arrivals
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // Nothing above touches global memory another grid may write: overlap it with that grid.
@@ -800,6 +834,100 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
       const uint32_t t_acc = t_lane + buf * Cfg::ACC_COLS;
       const int p = tp * Cfg::BM + row;
       const int q0 = tq * BN;
+
+      if (args.cluster_split > 1) {
+        // k-split inside a cluster: the S CTAs of this cluster hold the S k-slices of one tile
+        // (each CTA has exactly this one unit).  The tile's partial rows (rows of C's
+        // contiguous dimension) are dealt out to owners, rows [R r / S, R (r + 1) / S) to CTA
+        // r.  Once every CTA's mainloop is done (all operand rings idle), each CTA pushes each
+        // row of its fp32 partial into slot (its rank) of the owner's ring with remote
+        // stores; each owner then sums its rows over the S slots in rank order
+        // (deterministic) from its own shared memory and writes C.
+        const int S = args.cluster_split;
+        const int rk = (int)cluster_ctarank();
+        constexpr int PR = Cfg::PART_ROW;                // floats per partial row (+ pad)
+        constexpr int R = SWAP ? BN : Cfg::BM;           // partial rows (C rows of the tile)
+        const int rpo = (R + S - 1) / S;                 // slot height: most rows one owner has
+        const uint32_t part_s = smem_u32(smem);
+        // 1. this CTA's ring is idle: tell every CTA, then wait until every ring is
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+          for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(rfree_bar, j));
+        if (!mbar_wait_cluster(rfree_bar, 0, abort_flag, 8)) break;
+        // 2. push: partial row pr goes to owner o(pr) = the r with R r / S <= pr < R (r+1) / S
+        auto owner = [&](int pr) { return (int)(((pr + 1) * S - 1) / R); };
+#pragma unroll 1
+        for (int c = 0; c < BN / Cfg::CW; ++c) {
+          float f[32];
+          acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
+          if (SWAP) {
+            // lane = p (column of C), f[j] = partial row q = c * CW + j
+#pragma unroll
+            for (int j = 0; j < Cfg::CW; ++j) {
+              const int pr = c * Cfg::CW + j;
+              const int o = owner(pr);
+              const int lr = pr - R * o / S;
+              st_dsmem_f32(mapa_shared(part_s + (uint32_t)(((rk * rpo + lr) * PR + row) * 4), o),
+                           f[j]);
+            }
+          } else {
+            // lane = p (row of C), f = columns c * CW ... of that row
+            const int o = owner(row);
+            const int lr = row - R * o / S;
+            const uint32_t dst = mapa_shared(
+                part_s + (uint32_t)(((rk * rpo + lr) * PR + c * Cfg::CW) * 4), o);
+#pragma unroll
+            for (int k = 0; k < Cfg::CW / 4; ++k)
+              st_dsmem_f4(dst + 16 * k, make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2],
+                                                    f[4 * k + 3]));
+          }
+        }
+        tc_fence_before();
+        fence_acq_rel_cluster();  // this thread's remote stores before the warp's arrival
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(tempty_bar(buf));
+          for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(pready_bar, j));
+        }
+        if (!mbar_wait_cluster(pready_bar, 0, abort_flag, 9)) break;
+        // 3. owner: rows [lo, hi) of the tile, 4 columns per step, slots summed in rank order
+        const int lo = R * rk / S, hi = R * (rk + 1) / S;
+        constexpr int G = (SWAP ? Cfg::BM : BN) / 4;  // float4 groups per partial row
+        const float* part = reinterpret_cast<const float*>(smem);
+        const int m_rows = SWAP ? args.rows_q : args.rows_p;
+        const int n_cols = SWAP ? args.rows_p : args.rows_q;
+#pragma unroll 1
+        for (int i = threadIdx.x - 64; i < (hi - lo) * G; i += 128) {
+          const int lr = i / G, pc = (i - lr * G) * 4;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int j = 0; j < S; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(part + (j * rpo + lr) * PR + pc);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+          }
+          // C row m, first of 4 C columns n: swapped [q][p] -> (q0 + pr, p0 + pc)
+          const int pr = lo + lr;
+          const int m = SWAP ? q0 + pr : tp * Cfg::BM + pr;
+          const int n = SWAP ? tp * Cfg::BM + pc : q0 + pc;
+          if (m < m_rows && n < n_cols) {
+            if (WQ == kWInt8PerChannel) {
+              acc.x *= __half2float(__ldg(args.scale + n));
+              acc.y *= __half2float(__ldg(args.scale + n + 1));
+              acc.z *= __half2float(__ldg(args.scale + n + 2));
+              acc.w *= __half2float(__ldg(args.scale + n + 3));
+            }
+            uint2 w;
+            w.x = pack_half2(acc.x, acc.y);
+            w.y = pack_half2(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(args.C + (long long)m * args.ldc + n) = w;
+          }
+        }
+        continue;
+      }
 
       if (args.splits == 1 && !SWAP) {
         // fp16 tile through swizzled staging and TMA stores, 32 columns per box.

@@ -193,8 +193,12 @@ constexpr size_t kCounterBytes = (size_t)kMaxCounters * sizeof(int);  // 64 KiB
 // Bytes of the counter prefix that n counters occupy (what must be zero before a launch).
 size_t counters_used_bytes(int n) { return ((size_t)n * sizeof(int) + 255) / 256 * 256; }
 
+// k-splits up to this count run inside one cluster and reduce through distributed shared
+// memory (no workspace); larger counts go through the global workspace.
+constexpr int kMaxClusterSplit = kMaxClusterSplitDev;
+
 size_t ws_needed(int tiles, int splits, int bn) {
-  if (splits <= 1) return 0;
+  if (splits <= kMaxClusterSplit) return 0;
   if (tiles > kMaxCounters) return ~(size_t)0;
   return kCounterBytes + (size_t)tiles * splits * 128 * bn * sizeof(float);
 }
@@ -236,7 +240,8 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.group_m = std::max(1, h.group_m);
   a.C = static_cast<__half*>(pr.C);
   a.ldc = pr.ldc;
-  if (a.splits > 1) {
+  a.cluster_split = (a.splits > 1 && a.splits <= kMaxClusterSplit) ? a.splits : 0;
+  if (a.splits > kMaxClusterSplit) {
     if (!pr.ws || pr.ws_bytes < ws_needed(tiles, a.splits, BN)) return cudaErrorInvalidValue;
     a.counters = static_cast<int*>(pr.ws);
     a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
@@ -285,6 +290,9 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   }
   if (!ok) return cudaErrorInvalidValue;
 
+  if (a.cluster_split > 1)  // one CTA per unit, the k-slices of a tile in one cluster
+    return launch_ex(kern, dim3(a.num_units), dim3(Cfg::THREADS), Cfg::SMEM, st, a.splits, mP,
+                     mQ, mW, mC, mS, mZ, a);
   const int sms = dev_info(dev).sms;
   int grid = std::min(a.num_units, h.max_ctas > 0 ? h.max_ctas : sms);
   if (grid <= 0) return cudaErrorInvalidConfiguration;

@@ -48,8 +48,10 @@ HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, Fal
 
 
 @pytest.mark.parametrize("bn,swap", HYPER)
-@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("splits", [1, 3, 8, 10])
 def test_every_hyperform(dev, bn, swap, splits):
+    """splits 2..8 reduce inside a cluster through distributed shared memory, 10 through the
+    global workspace."""
     from cuda_tempiler_b200 import ops
     M, N, K = (24, 776, 1032) if swap else (260, 776, 1032)
     a, b, c = _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=bn, swap=swap, splits=splits,
@@ -106,10 +108,11 @@ def test_workspace_reuse_across_shapes(dev):
     problem leaves fp32 partials behind, then a 240-tile problem needs more counters than the
     first; the counters sit in a fixed prefix, so they never land on the old partials."""
     from cuda_tempiler_b200 import ops
-    big = lambda: _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=2,
+    # k-splits above the cluster limit (8) take the global workspace path
+    big = lambda: _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=10,
                                                             out=out), 16, 30720, 1024, seed=6)
     _gate(*big())  # sizes the cached workspace for both problems
-    small = _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=3,
+    small = _run(lambda A, B, out: ops.gemm_hyperform(A, B, bn=16, swap=True, splits=12,
                                                        out=out), 16, 3840, 4096, seed=5)
     _gate(*small)
     _gate(*big())
