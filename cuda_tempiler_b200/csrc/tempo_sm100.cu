@@ -70,7 +70,9 @@ int choose_splits(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, 
   if (sms <= 0) return 1;
   int best = 1;
   double best_c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, 1, hbm_bytes);
-  const int smax = std::min(32, num_kb / 2);
+  // the dispatcher keeps to cluster k-splits (the global-workspace path stays reachable as
+  // an explicit hyperform)
+  const int smax = std::min(kMaxClusterSplit, num_kb / 2);
   for (int s = 2; s <= smax; ++s) {
     if (ws_needed(tiles, s, bn) > ws_bytes) break;
     // a cluster k-split launch is one CTA per unit, not persistent: one wave only
@@ -174,6 +176,22 @@ int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, cons
                            int group_size, void* ws, size_t ws_bytes, void* stream) {
   if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, quant_kind, group_size))
     return cudaErrorInvalidConfiguration;
+  const int sms = current_sms();
+  if (M >= kExpandMinM && ws) {
+    // expanded weights at the front of the workspace, the fp16 launch's workspace behind them
+    const size_t wexp = expand_ws_bytes(N, K);
+    Hyper hf{};
+    if (ws_bytes >= wexp && select_hyper(0, M, N, K, ws_bytes - wexp, hf, sms)) {
+      cudaStream_t st = static_cast<cudaStream_t>(stream);
+      Problem pw{quant_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, wexp};
+      __half* wf = static_cast<__half*>(ws);
+      cudaError_t e = launch_expand(pw, wf, st);
+      if (e != cudaSuccess) return e;
+      Problem pr{0, A, wf, nullptr, nullptr, C, M, N, K, lda, K, ldc, 0,
+                 static_cast<char*>(ws) + wexp, ws_bytes - wexp};
+      return run(pr, hf, st);
+    }
+  }
   Hyper h{};
   if (!select_hyper(quant_kind, M, N, K, ws ? ws_bytes : 0, h, current_sms()))
     return cudaErrorInvalidConfiguration;
@@ -184,6 +202,10 @@ int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, cons
 size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind) {
   Hyper h{};
   const int sms = current_sms();
+  if (weight_kind != 0 && M >= kExpandMinM && (K % 16) == 0) {  // expanded weights + fp16 launch
+    if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, sms)) return 0;
+    return expand_ws_bytes(N, K) + hyper_ws(M, N, K, h, sms, (size_t)1 << 40, nullptr);
+  }
   if (!select_hyper(weight_kind, M, N, K, (size_t)1 << 40, h, sms)) return 0;
   return hyper_ws(M, N, K, h, sms, (size_t)1 << 40, nullptr);
 }
@@ -224,8 +246,13 @@ int tempo_sm100_pair_resources(int bn, int* out6) { return pair_resources(bn, ou
 
 int tempo_sm100_select(int weight_kind, int M, int N, int K, size_t ws_bytes, int* out5) {
   Hyper h{};
-  if (!select_hyper(weight_kind, M, N, K, ws_bytes, h, current_sms()))
+  const int sms = current_sms();
+  if (weight_kind != 0 && M >= kExpandMinM && ws_bytes >= expand_ws_bytes(N, K) &&
+      select_hyper(0, M, N, K, ws_bytes - expand_ws_bytes(N, K), h, sms)) {
+    weight_kind = 0;  // expanded weights: the fp16 launch's configuration
+  } else if (!select_hyper(weight_kind, M, N, K, ws_bytes, h, sms)) {
     return cudaErrorInvalidConfiguration;
+  }
   const InstEntry* e = find_inst(weight_kind, h.bn, h.swap);
   if (out5) {
     out5[0] = h.bn;

@@ -300,7 +300,7 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
                    mZ, a);
 }
 
-// Decode-sized streaming GEMV (hyperform bn == 0): M <= 4, 256 threads, R weight rows per warp.
+// Decode-sized streaming GEMV (hyperform bn == 0): M <= 16, 256 threads, R weight rows per warp.
 template <int WQ, int MM, int R>
 cudaError_t launch_gemv(const Problem& pr, cudaStream_t st) {
   const int rows_per_block = 8 * R;
@@ -316,10 +316,13 @@ template <int WQ, int R>
 cudaError_t gemv_by_m(const Problem& pr, cudaStream_t st) {
   if (pr.M == 1) return launch_gemv<WQ, 1, R>(pr, st);
   if (pr.M == 2) return launch_gemv<WQ, 2, R>(pr, st);
-  return launch_gemv<WQ, 4, R>(pr, st);
+  if (pr.M <= 4) return launch_gemv<WQ, 4, R>(pr, st);
+  // 8 and 16 activation rows: two weight rows per warp keep the accumulators in registers
+  if (pr.M <= 8) return launch_gemv<WQ, 8, 2>(pr, st);
+  return launch_gemv<WQ, 16, 2>(pr, st);
 }
 
-constexpr int kGemvMaxM = 4;
+constexpr int kGemvMaxM = 16;
 
 cudaError_t run_gemv(const Problem& pr, cudaStream_t st) {
   if (pr.M < 1 || pr.M > kGemvMaxM) return cudaErrorInvalidConfiguration;
@@ -330,6 +333,28 @@ cudaError_t run_gemv(const Problem& pr, cudaStream_t st) {
     case 2: return wide ? gemv_by_m<2, 4>(pr, st) : gemv_by_m<2, 2>(pr, st);
     default: return cudaErrorInvalidConfiguration;
   }
+}
+
+// W8A16 at prefill-sized M: expand the 8-bit weights to fp16 in the workspace, then the fp16
+// dispatch (2-CTA tiles) runs on the copy.  kExpandMinM and the workspace decide.
+constexpr int kExpandMinM = 512;
+
+size_t expand_ws_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 256; }
+
+cudaError_t launch_expand(const Problem& pr, __half* out, cudaStream_t st) {
+  const long long n = (long long)pr.N * (pr.K / 16);
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  const uint8_t* W = static_cast<const uint8_t*>(pr.W);
+  const __half* sc = static_cast<const __half*>(pr.scale);
+  const uint8_t* z = static_cast<const uint8_t*>(pr.zero);
+  const int g = pr.group > 0 ? pr.group : 16;
+  if (pr.wkind == kWInt8PerChannel)
+    return launch_ex(k_expand_w8<kWInt8PerChannel>, dim3(grid), dim3(256), 0, st, 1, W, sc, z,
+                     out, pr.N, pr.K, (long long)pr.ldw, g);
+  if (pr.wkind == kWUint8Group)
+    return launch_ex(k_expand_w8<kWUint8Group>, dim3(grid), dim3(256), 0, st, 1, W, sc, z, out,
+                     pr.N, pr.K, (long long)pr.ldw, g);
+  return cudaErrorInvalidConfiguration;
 }
 
 using LaunchFn = cudaError_t (*)(const Problem&, const Hyper&, cudaStream_t);

@@ -99,7 +99,7 @@ struct SkelCfg {
   // Independent accumulators per tile: a k-block's four 16-deep UMMAs rotate over NACC
   // accumulators so that narrow tiles (whose UMMAs are short) are not serialised on the
   // latency of accumulating into one TMEM region; the epilogue adds them up.
-  static constexpr int NACC = TA ? 1 : (BN <= 32 ? 4 : (BN <= 64 ? 2 : 1));
+  static constexpr int NACC = BN <= 32 ? 4 : (BN <= 64 ? 2 : 1);
   static constexpr int ACC_COLS = NACC * BN;  // TMEM columns of one accumulator buffer
   // as many A slots as TMEM leaves, a multiple of 2 x SUB (two dequant groups, SUB per stage)
   static constexpr int ASLOTS = TA ? cmin(16, ((512 - 2 * ACC_COLS) / 32) & ~3) : 1;
@@ -108,7 +108,9 @@ struct SkelCfg {
   static constexpr int NUM_WARPS = 6 + (TA ? 8 : (WQ ? 4 : 0));
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr int TMEM_COLS = TA ? 512 : tmem_cols_for(2 * ACC_COLS);
-  static constexpr int CW = BN < 32 ? 16 : 32;  // accumulator columns per tcgen05.ld
+  // accumulator columns per tcgen05.ld (16 where NACC x 32 columns would not fit the wide
+  // dequant CTAs' register budget)
+  static constexpr int CW = (BN < 32 || (TA && NACC > 2)) ? 16 : 32;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 is 16..256 step 16");
   static_assert(SWAP || BN >= 32, "non-swapped epilogue stores 32-column boxes");
   static_assert(STAGES >= 2, "pipeline needs at least two stages");
@@ -812,7 +814,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
 namespace tempo_sm100 {
 
 // ---------------------------------------------------------------------------------------------
-// k_gemv_sm100: the decode-sized (M <= 4) streaming GEMV, C[m][n] = sum_k A[m][k] * W[n][k].
+// k_gemv_sm100: the decode-sized (M <= 16) streaming GEMV, C[m][n] = sum_k A[m][k] * W[n][k].
 //
 // At M <= 16 a 128 x N x 16 UMMA costs about as much as a wide one, so the tensor-core path is
 // instruction-bound there; this kernel instead streams each weight row once with 16-byte
@@ -849,6 +851,41 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return v;
 }
 
+// k_expand_w8: the 8-bit weights of a W8A16 problem expanded to fp16 (W = q * s, or
+// (q - z) * s group-wise), 16 k per thread: 16 bytes in, 32 bytes out, streamed once.  For
+// prefill-sized M the tensor-core kernel then runs on fp16 weights at the full 2-CTA rate;
+// the pass costs 3 bytes per weight of HBM traffic, small against the GEMM at such M.
+template <int WQ>
+__global__ void __launch_bounds__(256)
+    k_expand_w8(const uint8_t* __restrict__ W, const __half* __restrict__ scale,
+                const uint8_t* __restrict__ zero, __half* __restrict__ out, int N, int K,
+                long long ldw, int group) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = K / 16;
+  if (i >= (long long)N * per_row) return;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = (int)(i / per_row);
+  const int k0 = (int)(i - (long long)n * per_row) * 16;
+  const uint4 x = ld_stream(W + (long long)n * ldw + k0);
+  __half2 zb = __float2half2_rn(0.f), s2 = zb;
+  if (WQ == kWUint8Group) {
+    const long long gi = (long long)(k0 / group) * N + n;
+    zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | __ldg(zero + gi))));
+    s2 = __half2half2(__ldg(scale + gi));
+  }
+  __half2 w[8];
+  gemv_weights<WQ>(x, w, zb, s2);
+  if (WQ == kWInt8PerChannel) {
+    const __half2 sc = __half2half2(__ldg(scale + n));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = __hmul2(w[j], sc);
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + (long long)n * K + k0);
+  o[0] = *reinterpret_cast<const uint4*>(&w[0]);
+  o[1] = *reinterpret_cast<const uint4*>(&w[4]);
+}
+
 template <int WQ, int MM, int R>
 __global__ void __launch_bounds__(256)
     k_gemv_sm100(const __half* __restrict__ A, const uint8_t* __restrict__ W,
@@ -857,6 +894,7 @@ __global__ void __launch_bounds__(256)
                  long long ldc, int group) {
   constexpr int ESZ = WQ ? 1 : 2;       // weight bytes per element
   constexpr int KC = 16 / ESZ;          // k per 16-byte chunk
+  constexpr int NW = KC / 2;            // packed fp16 pairs per chunk
   const int lane = threadIdx.x & 31;
   const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int n0 = warp_g * R;
@@ -879,32 +917,15 @@ __global__ void __launch_bounds__(256)
       const int n = min(n0 + r, N - 1);
       x[r] = ld_stream(W + (long long)n * ldw * ESZ + (long long)c * 16);
     }
-    __half2 a[MM][KC / 2];
-#pragma unroll
-    for (int m = 0; m < MM; ++m) {
-      if (m < M) {
-        const uint4* ap = reinterpret_cast<const uint4*>(A + (long long)m * lda + k0);
-#pragma unroll
-        for (int q = 0; q < KC / 8; ++q) {
-          const uint4 v = __ldg(ap + q);
-          a[m][4 * q + 0] = *reinterpret_cast<const __half2*>(&v.x);
-          a[m][4 * q + 1] = *reinterpret_cast<const __half2*>(&v.y);
-          a[m][4 * q + 2] = *reinterpret_cast<const __half2*>(&v.z);
-          a[m][4 * q + 3] = *reinterpret_cast<const __half2*>(&v.w);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < KC / 2; ++q) a[m][q] = __float2half2_rn(0.f);
-      }
-    }
+    // this chunk's weights of the R rows as packed fp16 pairs
+    __half2 w[R][8];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      __half2 w[8];
       if (WQ == kWFp16) {
-        w[0] = *reinterpret_cast<const __half2*>(&x[r].x);
-        w[1] = *reinterpret_cast<const __half2*>(&x[r].y);
-        w[2] = *reinterpret_cast<const __half2*>(&x[r].z);
-        w[3] = *reinterpret_cast<const __half2*>(&x[r].w);
+        w[r][0] = *reinterpret_cast<const __half2*>(&x[r].x);
+        w[r][1] = *reinterpret_cast<const __half2*>(&x[r].y);
+        w[r][2] = *reinterpret_cast<const __half2*>(&x[r].z);
+        w[r][3] = *reinterpret_cast<const __half2*>(&x[r].w);
       } else {
         __half2 zb = __float2half2_rn(0.f), s2 = zb;
         if (WQ == kWUint8Group) {
@@ -913,13 +934,34 @@ __global__ void __launch_bounds__(256)
           zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | __ldg(zero + gi))));
           s2 = __half2half2(__ldg(scale + gi));
         }
-        gemv_weights<WQ>(x[r], w, zb, s2);
+        gemv_weights<WQ>(x[r], w[r], zb, s2);
+      }
+    }
+    // one activation row at a time (its chunk is reused by the R weight rows), so the
+    // register footprint does not grow with MM
+#pragma unroll
+    for (int m = 0; m < MM; ++m) {
+      if (MM > 4 && m >= M) break;
+      __half2 a[NW];
+      if (MM <= 4 && m >= M) {
+#pragma unroll
+        for (int q = 0; q < NW; ++q) a[q] = __float2half2_rn(0.f);
+      } else {
+        const uint4* ap = reinterpret_cast<const uint4*>(A + (long long)m * lda + k0);
+#pragma unroll
+        for (int q = 0; q < KC / 8; ++q) {
+          const uint4 v = __ldg(ap + q);
+          a[4 * q + 0] = *reinterpret_cast<const __half2*>(&v.x);
+          a[4 * q + 1] = *reinterpret_cast<const __half2*>(&v.y);
+          a[4 * q + 2] = *reinterpret_cast<const __half2*>(&v.z);
+          a[4 * q + 3] = *reinterpret_cast<const __half2*>(&v.w);
+        }
       }
 #pragma unroll
-      for (int m = 0; m < MM; ++m) {
-        __half2 p = __hmul2(w[0], a[m][0]);
+      for (int r = 0; r < R; ++r) {
+        __half2 p = __hmul2(w[r][0], a[0]);
 #pragma unroll
-        for (int q = 1; q < KC / 2; ++q) p = __hfma2(w[q], a[m][q], p);
+        for (int q = 1; q < NW; ++q) p = __hfma2(w[r][q], a[q], p);
         const float2 f = __half22float2(p);
         acc[m][r] += f.x + f.y;
       }

@@ -37,7 +37,8 @@ BM, BK = 128, 64
 MAX_DYN_SMEM = 232448
 SWAP_BN = (16, 32, 64, 128)
 PREFILL_BN = (64, 128, 256)
-PAIR_BN = (256, 224, 192, 160, 128)  # 2-CTA tile widths (k_gemm_sm100_pair<BN>)
+PAIR_BN = (256, 224, 192, 160, 128)
+GEMV_MAX_M = 16  # the streaming GEMV (bn 0) covers M <= 16 (k_gemv_sm100 MM 1, 2, 4, 8, 16)  # 2-CTA tile widths (k_gemm_sm100_pair<BN>)
 SPLITS = (1, 2, 3, 4, 6, 8)
 
 
@@ -72,7 +73,7 @@ def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
     bar = 1024
     smem_stages = (MAX_DYN_SMEM - 1024 - epi - bar) // stage
     stages = (min(smem_stages, 24) & ~1) if ta else min(smem_stages, 12)
-    nacc = 1 if ta else (4 if bn <= 32 else (2 if bn <= 64 else 1))  # accumulators per tile
+    nacc = 4 if bn <= 32 else (2 if bn <= 64 else 1)  # accumulators per tile
     cols = 2 * bn * nacc
     tmem = 512 if ta else (32 if cols <= 32 else 1 << (cols - 1).bit_length())
     return dict(stage_bytes=stage, stages=stages, smem=1024 + stages * stage + epi + bar,
@@ -190,10 +191,11 @@ class Sm100Skeletons:
         M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
         num_kb = math.ceil(K / BK)
         forms, forms_out = [], []
-        if M <= 4:
+        if M <= GEMV_MAX_M:
+            mm = 1 if M == 1 else 2 if M == 2 else 4 if M <= 4 else 8 if M <= 8 else 16
             p = dict(family=FAMILY, bn=0, swap=0, splits=1, group_m=0, weight=wq, stages=0,
-                     cta_group=1, tmem_bufs=0, mm=1 if M == 1 else (2 if M == 2 else 4),
-                     rows=4 if N >= 9472 else 2)
+                     cta_group=1, tmem_bufs=0, mm=mm,
+                     rows=2 if mm > 4 else (4 if N >= 9472 else 2))
             if wq == 2:
                 p["group_size"] = group_size(op)
             forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))

@@ -88,7 +88,7 @@ def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=N
     rows = []
     cands = [(bn, True) for bn in HYPER["swap"] if M <= 256 or kind != 0] + \
         [(bn, False) for bn in HYPER["noswap"]]
-    if M <= 4:
+    if M <= 16:
         cands = [(0, False)] + cands  # the streaming GEMV
     if quick:  # only the tiles that can win at this M
         cands = [(bn, sw) for bn, sw in cands

@@ -106,10 +106,11 @@ def test_gptq_checkpoint_layout_end_to_end(dev):
     assert O.rel_l2(C.cpu().numpy(), ref) <= TOL
 
 
-@pytest.mark.parametrize("M", [1, 2, 3, 4])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 11, 16])
 @pytest.mark.parametrize("N,K", [(272, 512), (10240, 1024), (9472, 2064)])
 def test_streaming_gemv(dev, M, N, K):
-    """The CUDA-core streaming GEMV (hyperform bn=0, M <= 4) for all three weight kinds."""
+    """The CUDA-core streaming GEMV (hyperform bn=0, M <= 16: 1, 2, 4, 8 and 16 activation
+    rows per launch shape, ragged M inside each) for all three weight kinds."""
     from cuda_tempiler_b200 import ops
     r1 = _pc(M, N, K, lambda A, W, s, C: ops.gemm_hyperform(A, W, bn=0, swap=False, scale=s, out=C))
     G = 128 if K % 128 == 0 else 64 if K % 64 == 0 else 16
@@ -122,3 +123,20 @@ def test_streaming_gemv(dev, M, N, K):
     torch.cuda.synchronize()
     r3 = O.rel_l2(C.cpu().numpy(), O.gemm_fp16_ref(a, b))
     assert r1 <= TOL and r3 <= TOL, (r1, r3)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 1040, 2048), (1000, 2064, 1024), (2048, 5120, 5120)])
+def test_expand_path_prefill(dev, M, N, K):
+    """M >= 512 with a full workspace: the weights are expanded to fp16 in the workspace and
+    the 2-CTA fp16 kernel runs on the copy (per-channel and group-wise); without workspace the
+    same call takes the in-kernel dequant path.  Both pass the gate."""
+    from cuda_tempiler_b200 import ops
+    sel = ops.select(1, M, N, K)
+    assert sel["bn"] >= 128 and sel["swap"] == 0  # the fp16 2-CTA launch reports itself
+    r = _pc(M, N, K, lambda A, W, s, C: ops.gemm_w8a16(A, W, s, out=C))
+    assert r <= TOL, r
+    r = _pc(M, N, K, lambda A, W, s, C: ops.gemm_w8a16(A, W, s, out=C, use_workspace=False))
+    assert r <= TOL, r
+    r = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_w8a16(A, W, s, z, G, out=C))
+    assert r <= TOL, r
+    assert ops.device_status() == [0, 0, 0, 0]
