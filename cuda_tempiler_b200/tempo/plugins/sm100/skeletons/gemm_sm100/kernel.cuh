@@ -119,8 +119,8 @@ struct SkelCfg {
   // barriers: full[STAGES], empty[STAGES], deq[NDEQ] (indexed by stage, or by A slot for TA),
   // tmem full[2], tmem empty[2], done, aempty[ASLOTS]
   static constexpr int NDEQ = STAGES > ASLOTS ? STAGES : ASLOTS;
-  // + 2 for the cluster k-split: operand rings idle, partial rows delivered
-  static constexpr int NBARS = 2 * STAGES + NDEQ + 5 + ASLOTS + 2;
+  // + 3 for the cluster k-split: operand rings idle, partial rows delivered, deliveries done
+  static constexpr int NBARS = 2 * STAGES + NDEQ + 5 + ASLOTS + 3;
   static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
   // cluster k-split: an owner's S slots of partial rows in its idle operand ring, rows of C's
   // contiguous dimension ([q][p] swapped, [p][q] otherwise) padded by 4 floats; at most
@@ -128,6 +128,12 @@ struct SkelCfg {
   static constexpr int PART_ROW = (SWAP ? BM : BN) + 4;
   static_assert(((SWAP ? BN : BM) + kMaxClusterSplitDev) * PART_ROW * 4 <= STAGES * STAGE_BYTES,
                 "operand ring too small for the cluster k-split partial");
+  // Bulk exchange: this CTA's whole partial tile at the front of its ring and the owner slots
+  // behind it, where the ring holds both (every tile but the widest); else remote stores.
+  static constexpr int PART_SRC_BYTES = (SWAP ? BN : BM) * PART_ROW * 4;
+  static constexpr bool BULK_SPLIT =
+      PART_SRC_BYTES + ((SWAP ? BN : BM) + kMaxClusterSplitDev) * PART_ROW * 4 <=
+      STAGES * STAGE_BYTES;
 };
 
 __device__ __forceinline__ void decode_unit(const GemmArgs& a, int unit, int& tile, int& tp,
@@ -214,6 +220,7 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
   // cluster k-split: every CTA's operand ring idle / every CTA's partial rows delivered
   const uint32_t rfree_bar = bar_base + 8u * (kT0 + 5 + Cfg::ASLOTS);
   const uint32_t pready_bar = rfree_bar + 8u;
+  const uint32_t rdone_bar = rfree_bar + 16u;
   auto p_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::P_OFF; };
   auto q_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::Q_OFF; };
   auto raw_ptr = [&](int s) { return smem + s * Cfg::STAGE_BYTES + Cfg::RAW_OFF; };
@@ -236,7 +243,10 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
     for (int a = 0; a < Cfg::ASLOTS; ++a) mbar_init(aempty_bar(a), 1);
     const int csplit = args.cluster_split > 1 ? args.cluster_split : 1;
     mbar_init(rfree_bar, 4 * csplit);  // 4 epilogue warps of each CTA of the cluster
-    mbar_init(pready_bar, 4 * csplit);
+    // bulk exchange: the owner's own expect_tx arrival plus the slots' bytes; remote stores:
+    // the 4 epilogue warps of each CTA
+    mbar_init(pready_bar, Cfg::BULK_SPLIT ? 1 : 4 * csplit);
+    mbar_init(rdone_bar, csplit);  // each owner, once its slots are filled
     *abort_flag = 0;
     *last_flag = 0;
     fence_barrier_init();
@@ -413,62 +423,106 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
         // k-split inside a cluster: the S CTAs of this cluster hold the S k-slices of one tile
         // (each CTA has exactly this one unit).  The tile's partial rows (rows of C's
         // contiguous dimension) are dealt out to owners, rows [R r / S, R (r + 1) / S) to CTA
-        // r.  Once every CTA's mainloop is done (all operand rings idle), each CTA pushes each
-        // row of its fp32 partial into slot (its rank) of the owner's ring with remote
-        // stores; each owner then sums its rows over the S slots in rank order
+        // r.  Once every CTA's mainloop is done (all operand rings idle), each CTA delivers
+        // its fp32 rows into slot (its rank) of each owner's ring -- one bulk shared-to-shared
+        // copy per owner, or remote stores where the ring cannot hold the whole partial next
+        // to the slots -- and each owner sums its rows over the S slots in rank order
         // (deterministic) from its own shared memory and writes C.
         const int S = args.cluster_split;
         const int rk = (int)cluster_ctarank();
         constexpr int PR = Cfg::PART_ROW;                // floats per partial row (+ pad)
         constexpr int R = SWAP ? BN : Cfg::BM;           // partial rows (C rows of the tile)
         const int rpo = (R + S - 1) / S;                 // slot height: most rows one owner has
-        const uint32_t part_s = smem_u32(smem);
-        // 1. this CTA's ring is idle: tell every CTA, then wait until every ring is
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0)
-          for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(rfree_bar, j));
-        if (!mbar_wait_cluster(rfree_bar, 0, abort_flag, 8)) break;
-        // 2. push: partial row pr goes to owner o(pr) = the r with R r / S <= pr < R (r+1) / S
-        auto owner = [&](int pr) { return (int)(((pr + 1) * S - 1) / R); };
+        const uint32_t ring_s = smem_u32(smem);
+        // owner slots: behind the local partial (bulk exchange), or at the front of the ring
+        const uint32_t part_s = ring_s + (Cfg::BULK_SPLIT ? Cfg::PART_SRC_BYTES : 0);
+        auto lo_of = [&](int o) { return R * o / S; };
+        if (Cfg::BULK_SPLIT) {
+          // 1. the partial tile, [row][PR], into this CTA's own (idle) ring
+          float* src = reinterpret_cast<float*>(smem);
 #pragma unroll 1
-        for (int c = 0; c < BN / Cfg::CW; ++c) {
-          float f[32];
-          acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
-          if (SWAP) {
-            // lane = p (column of C), f[j] = partial row q = c * CW + j
+          for (int c = 0; c < BN / Cfg::CW; ++c) {
+            float f[32];
+            acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
+            if (SWAP) {
 #pragma unroll
-            for (int j = 0; j < Cfg::CW; ++j) {
-              const int pr = c * Cfg::CW + j;
-              const int o = owner(pr);
-              const int lr = pr - R * o / S;
-              st_dsmem_f32(mapa_shared(part_s + (uint32_t)(((rk * rpo + lr) * PR + row) * 4), o),
-                           f[j]);
+              for (int j = 0; j < Cfg::CW; ++j) src[(c * Cfg::CW + j) * PR + row] = f[j];
+            } else {
+#pragma unroll
+              for (int k = 0; k < Cfg::CW / 4; ++k)
+                *reinterpret_cast<float4*>(src + row * PR + c * Cfg::CW + 4 * k) =
+                    make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2], f[4 * k + 3]);
             }
-          } else {
-            // lane = p (row of C), f = columns c * CW ... of that row
-            const int o = owner(row);
-            const int lr = row - R * o / S;
-            const uint32_t dst = mapa_shared(
-                part_s + (uint32_t)(((rk * rpo + lr) * PR + c * Cfg::CW) * 4), o);
-#pragma unroll
-            for (int k = 0; k < Cfg::CW / 4; ++k)
-              st_dsmem_f4(dst + 16 * k, make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2],
-                                                    f[4 * k + 3]));
           }
+          tc_fence_before();
+          fence_proxy_async_smem();  // the bulk copies read it through the async proxy
+          __syncwarp();
+          // 2. every ring idle and every partial written: one thread sends each owner its rows
+          if (lane == 0) {
+            mbar_arrive(tempty_bar(buf));
+            for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(rfree_bar, j));
+          }
+          if (!mbar_wait_cluster(rfree_bar, 0, abort_flag, 8)) break;
+          if (threadIdx.x == 64) {
+            mbar_arrive_expect_tx(pready_bar,
+                                  (uint32_t)(S * (lo_of(rk + 1) - lo_of(rk)) * PR * 4));
+            for (int o = 0; o < S; ++o) {
+              const int rows = lo_of(o + 1) - lo_of(o);
+              bulk_copy_to_cluster(mapa_shared(part_s + (uint32_t)(rk * rpo * PR * 4), o),
+                                   ring_s + (uint32_t)(lo_of(o) * PR * 4),
+                                   (uint32_t)(rows * PR * 4), mapa_shared(pready_bar, o));
+            }
+          }
+          if (!mbar_wait_cluster(pready_bar, 0, abort_flag, 9)) break;
+        } else {
+          // 1. this CTA's ring is idle: tell every CTA, then wait until every ring is
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0)
+            for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(rfree_bar, j));
+          if (!mbar_wait_cluster(rfree_bar, 0, abort_flag, 8)) break;
+          // 2. push: partial row pr goes to owner o(pr) = the r with lo(r) <= pr < lo(r + 1)
+          auto owner = [&](int pr) { return (int)(((pr + 1) * S - 1) / R); };
+#pragma unroll 1
+          for (int c = 0; c < BN / Cfg::CW; ++c) {
+            float f[32];
+            acc_chunk<Cfg::CW, Cfg::NACC, BN>(t_acc, c, f);
+            if (SWAP) {
+              // lane = p (column of C), f[j] = partial row q = c * CW + j
+#pragma unroll
+              for (int j = 0; j < Cfg::CW; ++j) {
+                const int pr = c * Cfg::CW + j;
+                const int o = owner(pr);
+                const int lr = pr - lo_of(o);
+                st_dsmem_f32(
+                    mapa_shared(part_s + (uint32_t)(((rk * rpo + lr) * PR + row) * 4), o), f[j]);
+              }
+            } else {
+              // lane = p (row of C), f = columns c * CW ... of that row
+              const int o = owner(row);
+              const int lr = row - lo_of(o);
+              const uint32_t dst = mapa_shared(
+                  part_s + (uint32_t)(((rk * rpo + lr) * PR + c * Cfg::CW) * 4), o);
+#pragma unroll
+              for (int k = 0; k < Cfg::CW / 4; ++k)
+                st_dsmem_f4(dst + 16 * k, make_float4(f[4 * k], f[4 * k + 1], f[4 * k + 2],
+                                                      f[4 * k + 3]));
+            }
+          }
+          tc_fence_before();
+          fence_acq_rel_cluster();  // this thread's remote stores before the warp's arrival
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(tempty_bar(buf));
+            for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(pready_bar, j));
+          }
+          if (!mbar_wait_cluster(pready_bar, 0, abort_flag, 9)) break;
         }
-        tc_fence_before();
-        fence_acq_rel_cluster();  // this thread's remote stores before the warp's arrival
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(tempty_bar(buf));
-          for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(pready_bar, j));
-        }
-        if (!mbar_wait_cluster(pready_bar, 0, abort_flag, 9)) break;
         // 3. owner: rows [lo, hi) of the tile, 4 columns per step, slots summed in rank order
         const int lo = R * rk / S, hi = R * (rk + 1) / S;
         constexpr int G = (SWAP ? Cfg::BM : BN) / 4;  // float4 groups per partial row
-        const float* part = reinterpret_cast<const float*>(smem);
+        const float* part =
+            reinterpret_cast<const float*>(smem + (Cfg::BULK_SPLIT ? Cfg::PART_SRC_BYTES : 0));
         const int m_rows = SWAP ? args.rows_q : args.rows_p;
         const int n_cols = SWAP ? args.rows_p : args.rows_q;
 #pragma unroll 1
@@ -499,6 +553,12 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
             w.y = pack_half2(acc.z, acc.w);
             *reinterpret_cast<uint2*>(args.C + (long long)m * args.ldc + n) = w;
           }
+        }
+        if (Cfg::BULK_SPLIT && threadIdx.x == 64) {
+          // this CTA's slots are filled; it leaves only when every owner has filled its slots
+          // (so no copy still reads this CTA's partial)
+          for (int j = 0; j < S; ++j) mbar_arrive_cluster(mapa_shared(rdone_bar, j));
+          if (!mbar_wait_cluster(rdone_bar, 0, abort_flag, 10)) break;
         }
         continue;
       }

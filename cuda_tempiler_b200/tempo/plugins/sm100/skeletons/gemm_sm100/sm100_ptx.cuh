@@ -333,6 +333,17 @@ __device__ __forceinline__ void st_dsmem_f4(uint32_t cluster_addr, float4 v) {
                : "memory");
 }
 
+// Bulk copy from this CTA's shared memory into a CTA of the cluster (shared::cluster address),
+// completion counted as transaction bytes on that CTA's mbarrier.  16-byte aligned, size a
+// multiple of 16.  Not a multicast: one destination.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src_cta,
+                                                     uint32_t bytes, uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_acq_rel_cluster() {
   asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }
