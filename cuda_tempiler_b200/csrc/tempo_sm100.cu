@@ -95,6 +95,12 @@ bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int
   h.max_ctas = 0;
   h.cta_group = (wkind == 0 && r->cta_group == 2 && !r->swap) ? 2 : 1;
   const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
+  // a 128-wide 1-CTA row whose tiles overflow one wave takes the 256-wide tile (half the
+  // activation re-reads, one wave) when that instantiation exists
+  if (h.cta_group == 1 && !h.swap && h.bn == 128 && sms > 0 &&
+      (long long)((rows_p + 127) / 128) * ((rows_q + 127) / 128) > sms &&
+      find_inst(wkind, 256, 0) != nullptr)
+    h.bn = 256;
   const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
   const int num_kb = (K + 63) / 64;
   if (h.bn == 0) {  // streaming GEMV row of the ladder

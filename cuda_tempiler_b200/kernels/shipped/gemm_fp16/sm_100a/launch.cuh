@@ -337,7 +337,7 @@ cudaError_t run_gemv(const Problem& pr, cudaStream_t st) {
 
 // W8A16 at prefill-sized M: expand the 8-bit weights to fp16 in the workspace, then the fp16
 // dispatch (2-CTA tiles) runs on the copy.  kExpandMinM and the workspace decide.
-constexpr int kExpandMinM = 256;
+constexpr int kExpandMinM = 512;
 
 size_t expand_ws_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 256; }
 
