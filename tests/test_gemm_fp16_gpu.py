@@ -180,3 +180,16 @@ def test_dispatch_pair_width_by_waves(dev):
     assert ops.select(0, 4096, 30720, 3840)["bn"] == 256
     a, b, c = _run(ops.gemm_fp16, 1024, 3840, 15360, seed=3)
     _gate(a, b, c)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 248320, 512), (16, 248320, 512), (300, 248320, 256),
+                                   (1, 96, 5120), (16, 96, 5120), (1024, 96, 5120)])
+def test_lm_head_and_narrow_n(dev, M, N, K):
+    """Shapes outside the layer set: an lm_head-class wide N (248320 rows; K cut to keep the
+    CPU oracle's inputs small) and a narrow in-projection (N = 96), through the dispatcher."""
+    from cuda_tempiler_b200 import ops
+    a, b, c = _run(ops.gemm_fp16, M, N, K, seed=7)
+    assert O.poison_count(c) == 0
+    ref = O.gemm_fp16_ref(a, b)
+    assert O.rel_l2(c, ref) <= TOL
+    assert ops.device_status() == [0, 0, 0, 0]
