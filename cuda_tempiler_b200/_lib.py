@@ -44,7 +44,10 @@ EXPORTS = {
     "tempo_sm100_naive_gemm_w8a16": (
         _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "tempo_sm100_device_status": (_i, [_ip, _i]),
-    "tempo_sm100_silu_mul": (_i, [_vp, _vp, _i, _i, _i, _i, _vp]),
+    "tempo_sm100_silu_mul": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "tempo_sm100_gemm_fp16_swiglu": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "tempo_sm100_gemm_w8a16_swiglu": (
+        _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "tempo_sm100_version": (C.c_char_p, []),
     "tempo_sm100_gemm_fp16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
 }

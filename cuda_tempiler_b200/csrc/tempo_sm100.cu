@@ -309,12 +309,40 @@ int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale
 }
 
 int tempo_sm100_silu_mul(const void* gu, void* out, int M, int I, int ld_gu, int ld_out,
-                         void* stream) {
+                         int block, void* stream) {
   if (M <= 0 || I <= 0 || (I % 8) || (ld_gu % 8) || (ld_out % 8) || ld_gu < 2 * I || ld_out < I)
     return cudaErrorInvalidValue;
+  if (block < 0 || (block && ((block % 8) || (I % block)))) return cudaErrorInvalidValue;
   if (!aligned16(gu) || !aligned16(out)) return cudaErrorInvalidValue;
   return launch_silu_mul(static_cast<const __half*>(gu), static_cast<__half*>(out), M, I, ld_gu,
-                         ld_out, static_cast<cudaStream_t>(stream));
+                         ld_out, block, static_cast<cudaStream_t>(stream));
+}
+
+int tempo_sm100_gemm_fp16_swiglu(const void* A, const void* W, void* C, int M, int N, int K,
+                                 int lda, int ldw, int ldc, void* stream) {
+  if (M <= kSwigluMinM || N % 128 || !fp16_applicable(A, W, C, M, N / 2, K, lda, ldw, ldc))
+    return cudaErrorInvalidConfiguration;
+  if (ldw < K || (ldw % 8)) return cudaErrorInvalidConfiguration;
+  Problem pr{0, A, W, nullptr, nullptr, C, M, N, K, lda, ldw, ldc, 0, nullptr, 0};
+  return run_pair_swiglu(pr, current_sms(), static_cast<cudaStream_t>(stream));
+}
+
+int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scale,
+                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                                  int ldc, int quant_kind, int group_size, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  if (M < kExpandMinM || N % 128 || !ws || ws_bytes < expand_ws_bytes(N, K))
+    return cudaErrorInvalidConfiguration;
+  if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, N, quant_kind, group_size) ||
+      ldc < N / 2 || (ldc % 8))
+    return cudaErrorInvalidConfiguration;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Problem pw{quant_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
+  __half* wf = static_cast<__half*>(ws);
+  cudaError_t e = launch_expand(pw, wf, st);
+  if (e != cudaSuccess) return e;
+  Problem pr{0, A, wf, nullptr, nullptr, C, M, N, K, lda, K, ldc, 0, nullptr, 0};
+  return run_pair_swiglu(pr, current_sms(), st);
 }
 
 int tempo_sm100_device_status(int* out4, int reset) {

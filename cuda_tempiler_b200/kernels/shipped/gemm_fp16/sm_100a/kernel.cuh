@@ -1573,7 +1573,7 @@ struct PairCfg {
   static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
 };
 
-template <int BN>
+template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     k_gemm_sm100_pair(const __grid_constant__ CUtensorMap mapA,
                       const __grid_constant__ CUtensorMap mapB,
@@ -1834,8 +1834,53 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         continue;
       }
       const int live_cols = args.rows_q - q0;
-      const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
       const bool rows_live = row0 < args.rows_p;
+      if (SWIGLU) {
+        // Fused SwiGLU: the weight rows are gate/up blocks of 64 interleaved, so each 128
+        // accumulator columns of the tile hold 64 gate and the matching 64 up columns.  Out
+        // column j of group h: silu(acc[h*128 + j]) * acc[h*128 + 64 + j]; C has N / 2
+        // columns and this tile writes [q0 / 2, q0 / 2 + BN / 2).
+        const int groups = (live_cols >= BN ? BN : live_cols) / 128;
+#pragma unroll 1
+        for (int h = 0; h < groups; ++h) {
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            float g[32], u[32];
+            acc_chunk<32, 1, BN>(t_acc, h * 4 + cc, g);
+            acc_chunk<32, 1, BN>(t_acc, h * 4 + 2 + cc, u);
+            if (h == groups - 1 && cc == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+            }
+            if (!rows_live) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.f + expf(-g[j])) * u[j];
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            uint8_t* sbuf = stage_buf + sb * 2048;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint4 w;
+              w.x = pack_half2(g[8 * k + 0], g[8 * k + 1]);
+              w.y = pack_half2(g[8 * k + 2], g[8 * k + 3]);
+              w.z = pack_half2(g[8 * k + 4], g[8 * k + 5]);
+              w.w = pack_half2(g[8 * k + 6], g[8 * k + 7]);
+              const int pg = k ^ ((lane >> 1) & 3);  // 64-byte swizzle
+              *reinterpret_cast<uint4*>(sbuf + lane * 64 + pg * 16) = w;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&mapC, smem_u32(sbuf), q0 / 2 + h * 64 + cc * 32, row0);
+              bulk_commit_group();
+            }
+            sb ^= 1;
+          }
+        }
+        continue;
+      }
+      const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {
         float f[32];

@@ -436,10 +436,10 @@ PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool spli
 
 // 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs; h.splits > 1
 // allows the split tail of pair_plan.
-template <int BN>
+template <int BN, bool SWIGLU = false>
 cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   using Cfg = PairCfg<BN>;
-  auto kern = k_gemm_sm100_pair<BN>;
+  auto kern = k_gemm_sm100_pair<BN, SWIGLU>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -454,7 +454,10 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
   }
   if (pr.wkind != 0 || h.swap) return cudaErrorInvalidConfiguration;
-  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas, h.splits > 1,
+  if (SWIGLU && (pr.N % 128 || (BN != 128 && BN != 256))) return cudaErrorInvalidConfiguration;
+  // the fused SwiGLU epilogue has no split tail (its partial sums would be pre-activation)
+  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas,
+                                !SWIGLU && h.splits > 1,
                                 pr.ws ? pr.ws_bytes : 0);
   GemmArgs a{};
   a.rows_p = pr.M;
@@ -483,7 +486,8 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   bool ok = make_map(&mA, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
-  ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  ok &= make_map(&mC, pr.C, F16, 2, SWIGLU ? pr.N / 2 : pr.N, pr.M, pr.ldc, 32, 32,
+                 CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
   return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mB, mC,
                    a);
@@ -498,6 +502,23 @@ cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     case 128: return launch_pair<128>(pr, h, st);
     default: return cudaErrorInvalidConfiguration;
   }
+}
+
+// the fused SwiGLU GEMM covers prefill-sized M (the 2-CTA tiles); below it callers keep the
+// GEMM (GEMV / swap-AB tiles) and the separate SwiGLU kernel
+constexpr int kSwigluMinM = 256;
+
+// The fused SwiGLU 2-CTA launch (gate/up weight rows interleaved in blocks of 64, N even
+// multiple of 64, C [M][N / 2]): width 256 unless 128 fills the clusters better.
+cudaError_t run_pair_swiglu(const Problem& pr, int sms, cudaStream_t st) {
+  const int P = std::max(1, sms / 2);
+  const long long t256 = (long long)((pr.M + 255) / 256) * ((pr.N + 255) / 256);
+  const long long t128 = (long long)((pr.M + 255) / 256) * ((pr.N + 127) / 128);
+  const double c256 = (double)((t256 + P - 1) / P) * 256.0;
+  const double c128 = (double)((t128 + P - 1) / P) * 128.0 / 0.55;
+  Hyper h{c128 < c256 ? 128 : 256, 0, 1, 16, 0};
+  h.cta_group = 2;
+  return h.bn == 256 ? launch_pair<256, true>(pr, h, st) : launch_pair<128, true>(pr, h, st);
 }
 
 // Tile widths of the 2-CTA kernel, widest first, and their measured throughput per FLOP
@@ -537,11 +558,11 @@ void pair_facts(int* out6) {
 int pair_resources(int bn, int* out6) {
   const void* kern = nullptr;
   switch (bn) {
-    case 256: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<256>); pair_facts<256>(out6); break;
-    case 224: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<224>); pair_facts<224>(out6); break;
-    case 192: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<192>); pair_facts<192>(out6); break;
-    case 160: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<160>); pair_facts<160>(out6); break;
-    case 128: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<128>); pair_facts<128>(out6); break;
+    case 256: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<256, false>); pair_facts<256>(out6); break;
+    case 224: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<224, false>); pair_facts<224>(out6); break;
+    case 192: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<192, false>); pair_facts<192>(out6); break;
+    case 160: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<160, false>); pair_facts<160>(out6); break;
+    case 128: kern = reinterpret_cast<const void*>(&k_gemm_sm100_pair<128, false>); pair_facts<128>(out6); break;
     default: return cudaErrorInvalidConfiguration;
   }
   cudaFuncAttributes fa{};

@@ -169,15 +169,55 @@ def device_status(reset: bool = True) -> list:
     return list(out)
 
 
-def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """SwiGLU step: gu [M, 2I] holds [gate | up]; returns silu(gate) * up as [M, I] fp16."""
+def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None, block: int = 0) -> torch.Tensor:
+    """SwiGLU step: gu [M, 2I] holds [gate | up] (block 0) or gate and up alternating in blocks
+    of `block` columns; returns silu(gate) * up as [M, I] fp16."""
     lib = _lib.load()
     _check_2d(gu, "gu", torch.float16)
     M, I2 = gu.shape
     I = I2 // 2
     if out is None:
         out = torch.empty((M, I), dtype=torch.float16, device=gu.device)
-    rc = lib.tempo_sm100_silu_mul(_ptr(gu), _ptr(out), M, I, gu.stride(0), out.stride(0),
+    rc = lib.tempo_sm100_silu_mul(_ptr(gu), _ptr(out), M, I, gu.stride(0), out.stride(0), block,
                                   _stream(gu.device))
     _lib.check(rc, "tempo_sm100_silu_mul")
+    return out
+
+
+def gemm_fp16_swiglu(A: torch.Tensor, W: torch.Tensor,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(A Wg^T) * (A Wu^T) with gate/up rows of W interleaved in blocks of 64 (see
+    ``tp.interleave_rows``); raises NotCovered for M <= 256."""
+    lib = _lib.load()
+    _check_2d(A, "A", torch.float16)
+    _check_2d(W, "W", torch.float16)
+    M, K = A.shape
+    N = W.shape[0]
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=torch.float16, device=A.device)
+    rc = lib.tempo_sm100_gemm_fp16_swiglu(_ptr(A), _ptr(W), _ptr(out), M, N, K, A.stride(0),
+                                          W.stride(0), out.stride(0), _stream(A.device))
+    _lib.check(rc, "tempo_sm100_gemm_fp16_swiglu")
+    return out
+
+
+def gemm_w8a16_swiglu(A: torch.Tensor, W: torch.Tensor, scale: torch.Tensor,
+                      zero: torch.Tensor | None = None, group_size: int = 0,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """The W8A16 form of ``gemm_fp16_swiglu`` (rows, scales and zero points interleaved alike);
+    raises NotCovered below M = 512."""
+    lib = _lib.load()
+    _check_2d(A, "A", torch.float16)
+    M, K = A.shape
+    N = W.shape[0]
+    kind = W8_INT8_PER_CHANNEL if W.dtype == torch.int8 else W8_UINT8_GROUP
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=torch.float16, device=A.device)
+    ws = workspace(A.device, N * K * 2)
+    rc = lib.tempo_sm100_gemm_w8a16_swiglu(
+        _ptr(A), _ptr(W), _ptr(scale.contiguous()),
+        _ptr(zero.contiguous() if zero is not None else None), _ptr(out), M, N, K, A.stride(0),
+        W.stride(0), out.stride(0), kind, group_size, _ptr(ws), 0 if ws is None else ws.numel(),
+        _stream(A.device))
+    _lib.check(rc, "tempo_sm100_gemm_w8a16_swiglu")
     return out

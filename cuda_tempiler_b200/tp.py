@@ -2,8 +2,10 @@
 ranks of a process group, one process per GPU.
 
     gate_up  column-parallel: rank r holds gate rows [r I/tp, (r+1) I/tp) and the matching up
-             rows, stacked as one [2 I/tp, H] weight, so its GEMM output [M, 2 I/tp] is
-             [gate_r | up_r] and SiLU(gate_r) * up_r needs no communication;
+             rows as one [2 I/tp, H] weight, interleaved in blocks of 64 rows (gate 64, up 64,
+             ...) when I/tp is a multiple of 64, else stacked [gate_r | up_r], so SiLU(gate)
+             * up needs no communication; with the interleaved layout the SwiGLU step runs in
+             the gate_up GEMM's epilogue at prefill sizes (``ops.gemm_*_swiglu``);
     down     row-parallel: rank r holds W_down[:, r I/tp : (r+1) I/tp] as a K-contiguous
              [H, I/tp] weight and produces a partial [M, H];
     reduce   one all-reduce (sum) of the fp16 [M, H] partial -- the only exchange step.
@@ -19,6 +21,31 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import torch
+
+
+GU_BLOCK = 64  # gate/up interleave block of the fused SwiGLU epilogue
+
+
+def interleave_rows(a: torch.Tensor, b: torch.Tensor, block: int) -> torch.Tensor:
+    """[a rows 0..block) | b rows 0..block) | a rows block..2 block) | ...] along dim 0."""
+    n = a.shape[0]
+    if n % block or b.shape != a.shape:
+        raise ValueError(f"{tuple(a.shape)} / {tuple(b.shape)} do not interleave in blocks of {block}")
+    rest = tuple(a.shape[1:])
+    return torch.stack([a.reshape(n // block, block, *rest), b.reshape(n // block, block, *rest)],
+                       1).reshape(2 * n, *rest)
+
+
+def swiglu_ref(gu: torch.Tensor, block: int) -> torch.Tensor:
+    """fp32 silu(gate) * up of a gate_up output in either layout (block 0: [gate | up])."""
+    M, I2 = gu.shape
+    I = I2 // 2
+    if block:
+        v = gu.float().reshape(M, I // block, 2, block)
+        g, u = v[:, :, 0, :].reshape(M, I), v[:, :, 1, :].reshape(M, I)
+    else:
+        g, u = gu[:, :I].float(), gu[:, I:].float()
+    return g * torch.sigmoid(g) * u
 
 
 def shard_rows(n_total: int, world: int, rank: int) -> slice:
@@ -37,15 +64,22 @@ class MLPShard:
     w_down: torch.Tensor
     s_down: torch.Tensor | None
     inter: int  # I / tp, the intermediate columns this rank owns
+    gu_block: int = 0  # GU_BLOCK: gate/up rows interleaved in blocks of 64; 0: [gate | up]
 
 
 def shard_mlp(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, world: int,
               rank: int, s_gate=None, s_up=None, s_down=None) -> MLPShard:
     """Cut full weights (gate/up [I, H], down [H, I]) into rank `rank`'s shard."""
     sl = shard_rows(w_gate.shape[0], world, rank)
-    wgu = torch.cat([w_gate[sl], w_up[sl]], 0).contiguous()
-    sgu = None if s_gate is None else torch.cat([s_gate[sl], s_up[sl]], 0).contiguous()
-    return MLPShard(wgu, sgu, w_down[:, sl].contiguous(), s_down, sl.stop - sl.start)
+    inter = sl.stop - sl.start
+    block = GU_BLOCK if inter % GU_BLOCK == 0 else 0
+    if block:
+        wgu = interleave_rows(w_gate[sl], w_up[sl], block).contiguous()
+        sgu = None if s_gate is None else interleave_rows(s_gate[sl], s_up[sl], block).contiguous()
+    else:
+        wgu = torch.cat([w_gate[sl], w_up[sl]], 0).contiguous()
+        sgu = None if s_gate is None else torch.cat([s_gate[sl], s_up[sl]], 0).contiguous()
+    return MLPShard(wgu, sgu, w_down[:, sl].contiguous(), s_down, inter, block)
 
 
 def _default_gemm(x, w, s):
@@ -55,18 +89,36 @@ def _default_gemm(x, w, s):
     return ops.gemm_w8a16(x, w, s)
 
 
-def _default_swiglu(gu):
+def _default_swiglu(gu, block):
     from . import ops
-    return ops.silu_mul(gu)
+    return ops.silu_mul(gu, block=block)
+
+
+def _default_fused(x, w, s):
+    """The gate_up GEMM with SwiGLU in its epilogue, or None where it does not cover M."""
+    from . import ops
+    from ._lib import NotCovered
+    try:
+        if w.dtype == torch.float16:
+            return ops.gemm_fp16_swiglu(x, w)
+        return ops.gemm_w8a16_swiglu(x, w, s)
+    except NotCovered:
+        return None
 
 
 def mlp_forward(x: torch.Tensor, shard: MLPShard, group=None, gemm=None, swiglu=None,
-                all_reduce=True) -> torch.Tensor:
-    """y = down(silu(gate(x)) * up(x)) for this rank's shard, summed over the group."""
+                all_reduce=True, fused=None) -> torch.Tensor:
+    """y = down(silu(gate(x)) * up(x)) for this rank's shard, summed over the group.  With the
+    library's own GEMM (gemm None) and an interleaved shard the fused gate_up + SwiGLU kernel
+    runs where it covers M; ``fused=False`` keeps the two-kernel path."""
+    if fused is None:
+        fused = _default_fused if gemm is None else False
     gemm = gemm or _default_gemm
     swiglu = swiglu or _default_swiglu
-    gu = gemm(x, shard.w_gate_up, shard.s_gate_up)       # [M, 2 I/tp]
-    h = swiglu(gu)                                        # [M, I/tp]
+    h = fused(x, shard.w_gate_up, shard.s_gate_up) if (fused and shard.gu_block) else None
+    if h is None:
+        gu = gemm(x, shard.w_gate_up, shard.s_gate_up)   # [M, 2 I/tp]
+        h = swiglu(gu, shard.gu_block)                    # [M, I/tp]
     y = gemm(h, shard.w_down, shard.s_down)               # [M, H] partial
     if all_reduce:
         import torch.distributed as dist

@@ -112,11 +112,27 @@ int tempo_sm100_naive_gemm_w8a16(const void* A, const void* W, const void* scale
                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
                                  int ldc, int quant_kind, int group_size, void* stream);
 
-/* out[m][i] = silu(gu[m][i]) * gu[m][I + i] for a gate_up GEMM output whose row m holds the
- * gate half [0, I) and the up half [I, 2I) (the SwiGLU step of the tensor-parallel MLP; the
- * reference names this elementwise cost but has no kernel for it).  fp16, I % 8 == 0. */
+/* out[m][i] = silu(gate) * up for a gate_up GEMM output row m (the SwiGLU step of the
+ * tensor-parallel MLP; the reference names this elementwise cost but has no kernel for it).
+ * block 0: the row holds the gate half [0, I) and the up half [I, 2I); block b > 0: gate and
+ * up alternate in blocks of b columns (the interleaved layout of the fused entry points below).
+ * fp16, I % 8 == 0, b % 8 == 0 and I % b == 0. */
 int tempo_sm100_silu_mul(const void* gu, void* out, int M, int I, int ld_gu, int ld_out,
-                         void* stream);
+                         int block, void* stream);
+
+/* gate_up GEMM with the SwiGLU step fused into its epilogue (reference: the fusion its notes
+ * name as next, tempo/plugins/sm70/__init__.py:66).  W [N][K] holds the gate and up weight rows
+ * interleaved in blocks of 64 (rows 128 t + j: gate row 64 t + j; rows 128 t + 64 + j: up row
+ * 64 t + j), N = 2 I a multiple of 128; C [M][I] = silu(A Wg^T) * (A Wu^T), ldc >= I.  Covers
+ * M > 256 (2-CTA tiles); 9 below, where the GEMM plus tempo_sm100_silu_mul (block 64) is the
+ * caller's path.  The W8A16 form (same quantisation arguments as tempo_sm100_gemm_w8a16, scales
+ * and zero points permuted like the rows) covers M >= 512 with ws >= N * K * 2 bytes. */
+int tempo_sm100_gemm_fp16_swiglu(const void* A, const void* W, void* C, int M, int N, int K,
+                                 int lda, int ldw, int ldc, void* stream);
+int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scale,
+                                  const void* zero, void* C, int M, int N, int K, int lda, int ldw,
+                                  int ldc, int quant_kind, int group_size, void* ws,
+                                  size_t ws_bytes, void* stream);
 
 /* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
  * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the

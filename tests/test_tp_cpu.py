@@ -26,10 +26,9 @@ def _oracle_gemm(x, w, s):
     return y
 
 
-def _oracle_swiglu(gu):
-    I = gu.shape[1] // 2
-    g, u = gu[:, :I].float(), gu[:, I:].float()
-    return g * torch.sigmoid(g) * u
+def _oracle_swiglu(gu, block):
+    from cuda_tempiler_b200 import tp
+    return tp.swiglu_ref(gu, block)
 
 
 def _weights(H, I, seed=0):

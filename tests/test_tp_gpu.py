@@ -41,7 +41,58 @@ def _oracle_mlp(x, wg, wu, wd, sg, su, sd):
     return h @ (wd.float().cpu().numpy() * sd.float().cpu().numpy()[:, None]).T
 
 
-@pytest.mark.parametrize("M", [1, 16, 256])
+def test_silu_mul_kernel_interleaved(dev):
+    """The block-interleaved layout (gate 64 | up 64 | ...) of the fused entry points."""
+    from cuda_tempiler_b200 import ops, tp
+    g = torch.Generator(device="cuda").manual_seed(1)
+    gu = torch.randn(19, 2 * 320, generator=g, device="cuda").half()
+    out = ops.silu_mul(gu, block=64)
+    ref = tp.swiglu_ref(gu, 64)
+    assert O.rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < 1e-3
+
+
+def _swiglu_oracle(a, wg, wu):
+    g = a.astype(np.float32) @ wg.astype(np.float32).T
+    u = a.astype(np.float32) @ wu.astype(np.float32).T
+    return g / (1 + np.exp(-g)) * u
+
+
+@pytest.mark.parametrize("M,I,K", [(300, 512, 1024), (1024, 1536, 2048), (2048, 2176, 512)])
+def test_fused_swiglu_fp16(dev, M, I, K):
+    """gate_up GEMM with SwiGLU in the 2-CTA epilogue against silu(A Wg^T) * (A Wu^T)."""
+    from cuda_tempiler_b200 import ops, tp
+    a, wg = O.inputs_layer(M, I, K, seed=11)
+    _, wu = O.inputs_layer(M, I, K, seed=12)
+    W = tp.interleave_rows(torch.from_numpy(wg), torch.from_numpy(wu), 64).cuda()
+    C = torch.empty((M, I), dtype=torch.float16, device="cuda")
+    C.view(torch.int16).fill_(0x7F7F)
+    ops.gemm_fp16_swiglu(torch.from_numpy(a).cuda(), W, out=C)
+    torch.cuda.synchronize()
+    c = C.cpu().numpy()
+    assert O.poison_count(c) == 0
+    assert O.rel_l2(c, _swiglu_oracle(a, wg, wu)) <= O.GATE_REL_L2
+    assert ops.device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("M", [512, 1024])
+def test_fused_swiglu_w8a16(dev, M):
+    """The W8A16 form: per-channel weights and scales interleaved alike, expanded, fused."""
+    from cuda_tempiler_b200 import ops, tp
+    I, K = 1024, 1536
+    a, qg, sg = O.inputs_w8_per_channel(M, I, K, 21)
+    _, qu, su = O.inputs_w8_per_channel(M, I, K, 22)
+    W = tp.interleave_rows(torch.from_numpy(qg), torch.from_numpy(qu), 64).cuda()
+    S = tp.interleave_rows(torch.from_numpy(sg), torch.from_numpy(su), 64).cuda()
+    C = ops.gemm_w8a16_swiglu(torch.from_numpy(a).cuda(), W, S)
+    torch.cuda.synchronize()
+    ref = _swiglu_oracle(a, O.dequant_per_channel(qg, sg), O.dequant_per_channel(qu, su))
+    assert O.rel_l2(C.cpu().numpy(), ref) <= O.GATE_REL_L2
+    from cuda_tempiler_b200._lib import NotCovered
+    with pytest.raises(NotCovered):
+        ops.gemm_w8a16_swiglu(torch.from_numpy(a[:16]).cuda(), W, S)
+
+
+@pytest.mark.parametrize("M", [1, 16, 256, 1024])
 def test_mlp_single_rank(dev, M):
     from cuda_tempiler_b200 import tp
     x, wg, wu, wd, sg, su, sd = _mlp_inputs(M, 512, 1024, dev)
