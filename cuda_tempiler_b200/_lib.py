@@ -48,6 +48,12 @@ EXPORTS = {
     "tempo_sm100_gemm_fp16_swiglu": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "tempo_sm100_gemm_w8a16_swiglu": (
         _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "tempo_sm100_ipc_handle": (_i, [_vp, _vp]),
+    "tempo_sm100_ipc_open": (_i, [_vp, C.POINTER(C.c_void_p)]),
+    "tempo_sm100_ipc_close": (_i, [_vp]),
+    "tempo_sm100_allreduce_oneshot": (
+        _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+             _i, _i, C.c_uint, _i, _vp]),
     "tempo_sm100_version": (C.c_char_p, []),
     "tempo_sm100_gemm_fp16_noalloc": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
 }

@@ -15,6 +15,7 @@
 #include "tempo_sm100.h"
 #include "launch.cuh"
 #include "elementwise.cuh"
+#include "collective.cuh"
 
 namespace tempo_sm100 {
 namespace {
@@ -343,6 +344,42 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
   if (e != cudaSuccess) return e;
   Problem pr{0, A, wf, nullptr, nullptr, C, M, N, K, lda, K, ldc, 0, nullptr, 0};
   return run_pair_swiglu(pr, current_sms(), st);
+}
+
+int tempo_sm100_ipc_handle(const void* dptr, void* out_handle) {
+  if (!dptr || !out_handle) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dptr));
+  if (e == cudaSuccess) std::memcpy(out_handle, &h, sizeof(h));
+  return e;
+}
+
+int tempo_sm100_ipc_open(const void* handle, void** out_ptr) {
+  if (!handle || !out_ptr) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(out_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int tempo_sm100_ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr); }
+
+int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,
+                                  void* const* recv, void* const* flags, int tp, int rank,
+                                  unsigned epoch, int ctas, void* stream) {
+  if (!src || !dst || !recv || !flags || tp < 1 || tp > kArMaxTp || rank < 0 || rank >= tp)
+    return cudaErrorInvalidValue;
+  if (n <= 0 || (n % 8) || n > cap || (cap % 8) || ctas < 1 || ctas > kArMaxCtas || epoch == 0)
+    return cudaErrorInvalidValue;
+  if (!aligned16(src) || !aligned16(dst)) return cudaErrorInvalidValue;
+  PeerSet ps{};
+  for (int p = 0; p < tp; ++p) {
+    if (!recv[p] || !flags[p] || !aligned16(recv[p])) return cudaErrorInvalidValue;
+    ps.recv[p] = static_cast<__half*>(recv[p]);
+    ps.flags[p] = static_cast<uint32_t*>(flags[p]);
+  }
+  return launch_ex(k_allreduce_oneshot, dim3(ctas), dim3(256), 0,
+                   static_cast<cudaStream_t>(stream), 1, static_cast<const __half*>(src),
+                   static_cast<__half*>(dst), n, cap, ps, tp, rank, (uint32_t)epoch);
 }
 
 int tempo_sm100_device_status(int* out4, int reset) {

@@ -8,7 +8,9 @@ ranks of a process group, one process per GPU.
              the gate_up GEMM's epilogue at prefill sizes (``ops.gemm_*_swiglu``);
     down     row-parallel: rank r holds W_down[:, r I/tp : (r+1) I/tp] as a K-contiguous
              [H, I/tp] weight and produces a partial [M, H];
-    reduce   one all-reduce (sum) of the fp16 [M, H] partial -- the only exchange step.
+    reduce   one all-reduce (sum) of the fp16 [M, H] partial -- the only exchange step: NCCL,
+             or for decode-sized M the library's one-shot all-reduce over peer memory
+             (``PeerAllReduce``).
 
 The reference is single-GPU (it has no multi-GPU code); this helper is new.  Each GEMM is the
 sm_100a kernel (``ops.gemm_w8a16`` / ``ops.gemm_fp16``); the SwiGLU step is the library's
@@ -106,6 +108,83 @@ def _default_fused(x, w, s):
         return None
 
 
+class PeerAllReduce:
+    """One-shot all-reduce (sum) of fp16 vectors up to `cap` values over the ranks of `group`
+    through peer memory (``tempo_sm100_allreduce_oneshot``: every rank stores its vector into
+    every rank's receive buffer, raises a flag there, waits for all flags and sums in rank
+    order).  For the decode-sized down-projection partial; longer vectors fall back to
+    ``torch.distributed.all_reduce``.  Buffers are exchanged once, by CUDA IPC handles
+    all-gathered over the process group; all ranks must be on one node."""
+
+    def __init__(self, cap: int, group=None, device=None, ctas: int = 16):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from . import _lib
+        self._lib = _lib.load()
+        self.group = group
+        self.tp = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.tp > 8:
+            raise ValueError("the one-shot all-reduce covers up to 8 ranks")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.cap = -(-cap // 8) * 8
+        self.ctas = ctas
+        self.recv = torch.zeros(2 * self.tp * self.cap, dtype=torch.float16, device=self.device)
+        self.flags = torch.zeros(self.tp * 32, dtype=torch.int32, device=self.device)
+        hr, hf = (C.c_uint8 * 64)(), (C.c_uint8 * 64)()
+        _lib.check(self._lib.tempo_sm100_ipc_handle(self.recv.data_ptr(), hr), "ipc_handle")
+        _lib.check(self._lib.tempo_sm100_ipc_handle(self.flags.data_ptr(), hf), "ipc_handle")
+        mine = torch.tensor(list(bytes(hr)) + list(bytes(hf)), dtype=torch.uint8,
+                            device=self.device)
+        every = [torch.empty_like(mine) for _ in range(self.tp)]
+        dist.all_gather(every, mine, group=group)
+        self._opened = []
+        rp, fp = [], []
+        for p, t in enumerate(every):
+            if p == self.rank:
+                rp.append(self.recv.data_ptr())
+                fp.append(self.flags.data_ptr())
+                continue
+            raw = bytes(t.cpu().tolist())
+            ptrs = []
+            for h in (raw[:64], raw[64:]):
+                out = C.c_void_p()
+                buf = (C.c_uint8 * 64).from_buffer_copy(h)
+                _lib.check(self._lib.tempo_sm100_ipc_open(buf, C.byref(out)), "ipc_open")
+                self._opened.append(out.value)
+                ptrs.append(out.value)
+            rp.append(ptrs[0])
+            fp.append(ptrs[1])
+        self._recv_ptrs = (C.c_void_p * self.tp)(*rp)
+        self._flag_ptrs = (C.c_void_p * self.tp)(*fp)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def __call__(self, y: torch.Tensor) -> torch.Tensor:
+        """In place: y <- sum of y over the ranks."""
+        import torch.distributed as dist
+
+        from . import _lib
+        n = y.numel()
+        if y.dtype != torch.float16 or not y.is_contiguous() or n % 8 or n > self.cap:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+            return y
+        self.epoch += 1
+        rc = self._lib.tempo_sm100_allreduce_oneshot(
+            y.data_ptr(), y.data_ptr(), n, self.cap, self._recv_ptrs, self._flag_ptrs, self.tp,
+            self.rank, self.epoch, self.ctas, torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "tempo_sm100_allreduce_oneshot")
+        return y
+
+    def close(self):
+        for p in self._opened:
+            self._lib.tempo_sm100_ipc_close(p)
+        self._opened = []
+
+
 def mlp_forward(x: torch.Tensor, shard: MLPShard, group=None, gemm=None, swiglu=None,
                 all_reduce=True, fused=None) -> torch.Tensor:
     """y = down(silu(gate(x)) * up(x)) for this rank's shard, summed over the group.  With the
@@ -120,6 +199,8 @@ def mlp_forward(x: torch.Tensor, shard: MLPShard, group=None, gemm=None, swiglu=
         gu = gemm(x, shard.w_gate_up, shard.s_gate_up)   # [M, 2 I/tp]
         h = swiglu(gu, shard.gu_block)                    # [M, I/tp]
     y = gemm(h, shard.w_down, shard.s_down)               # [M, H] partial
+    if callable(all_reduce):                              # e.g. a PeerAllReduce
+        return all_reduce(y)
     if all_reduce:
         import torch.distributed as dist
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:

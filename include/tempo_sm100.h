@@ -134,6 +134,25 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
                                   int ldc, int quant_kind, int group_size, void* ws,
                                   size_t ws_bytes, void* stream);
 
+/* Peer memory for the tensor-parallel exchange (one process per GPU of one node): the 64-byte
+ * CUDA IPC handle of a device allocation, its mapping in another process, and the unmapping. */
+#define TEMPO_SM100_IPC_HANDLE_BYTES 64
+int tempo_sm100_ipc_handle(const void* dptr, void* out_handle);
+int tempo_sm100_ipc_open(const void* handle, void** out_ptr);
+int tempo_sm100_ipc_close(void* ptr);
+
+/* One-shot all-reduce (sum) of n fp16 values over tp <= 8 ranks through peer memory, for the
+ * decode-sized partial of the row-parallel down projection (no counterpart in the reference,
+ * which is single-GPU; NCCL's all-reduce is the general path).  recv[p] / flags[p]: rank p's
+ * receive buffer (2 * tp * cap fp16, 16-byte aligned) and flag array (tp * 32 uint32, zeroed
+ * once), as mapped in this process (this rank's own at p == rank).  epoch: 1, 2, 3, ... per
+ * call, the same on every rank.  ctas <= 32 CTAs split the vector.  Every rank must make the
+ * same call; a rank that does not arrive within 2 s leaves status 1 (role 20) in
+ * tempo_sm100_device_status and the output undefined.  n % 8 == 0, n <= cap. */
+int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,
+                                  void* const* recv, void* const* flags, int tp, int rank,
+                                  unsigned epoch, int ctas, void* stream);
+
 /* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
  * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the
  * current device. */

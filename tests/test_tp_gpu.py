@@ -137,3 +137,94 @@ def test_mlp_two_ranks_nccl():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert O.rel_l2(y, ref) <= O.GATE_REL_L2
+
+
+def test_allreduce_oneshot_emulated_ranks(dev):
+    """The one-shot all-reduce kernel's data path and flags for tp = 3 on one GPU: the other two
+    ranks' slots and flags are filled beforehand (so the kernel waits on nothing another launch
+    would have to provide), rank 0 pushes, flags, waits and sums; bit-identical to the rank-order
+    fp32 sum, for both call parities."""
+    import ctypes as C
+    from cuda_tempiler_b200 import _lib
+    lib = _lib.load()
+    tp, cap, n, ctas = 3, 4096, 3000, 8
+    g = torch.Generator(device="cuda").manual_seed(5)
+    recv = [torch.zeros(2 * tp * cap, dtype=torch.float16, device="cuda") for _ in range(tp)]
+    flags = [torch.zeros(tp * 32, dtype=torch.int32, device="cuda") for _ in range(tp)]
+    rp = (C.c_void_p * tp)(*[t.data_ptr() for t in recv])
+    fp = (C.c_void_p * tp)(*[t.data_ptr() for t in flags])
+    for epoch in (1, 2):
+        xs = [torch.randn(n, generator=g, device="cuda").half() for _ in range(tp)]
+        half = (epoch & 1) * tp * cap
+        for s in (1, 2):  # ranks 1 and 2 have already delivered into rank 0
+            recv[0][half + s * cap: half + s * cap + n] = xs[s]
+            flags[0][s * 32: s * 32 + ctas] = epoch
+        y = xs[0].clone()
+        rc = lib.tempo_sm100_allreduce_oneshot(y.data_ptr(), y.data_ptr(), n, cap, rp, fp, tp, 0,
+                                               epoch, ctas, torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        ref = (xs[0].float() + xs[1].float() + xs[2].float()).half()
+        assert torch.equal(y, ref)
+        for p in range(tp):  # rank 0's slice landed in every rank's slot 0, flags raised
+            assert torch.equal(recv[p][half: half + n], xs[0])
+            assert bool((flags[p][0:ctas] == epoch).all())
+    assert ops_status() == [0, 0, 0, 0]
+
+
+def ops_status():
+    from cuda_tempiler_b200 import ops
+    return ops.device_status()
+
+
+def _peer_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    from cuda_tempiler_b200 import ops, tp
+    par = tp.PeerAllReduce(16 * 5120)
+    ok = True
+    for it in range(5):
+        g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
+        y = torch.randn(16 * 5120, generator=g, device="cuda").half()
+        ref = y.clone()
+        dist.all_reduce(ref)
+        par(y)
+        torch.cuda.synchronize()
+        ok &= bool(torch.allclose(y.float(), ref.float(), rtol=2e-3, atol=2e-3))
+    # the MLP through the peer exchange equals the NCCL one
+    x, wg, wu, wd, sg, su, sd = _mlp_inputs(16, 512, 1024, torch.device("cuda", rank))
+    sh = tp.shard_mlp(wg, wu, wd, world, rank, sg, su, sd)
+    y1 = tp.mlp_forward(x, sh, all_reduce=par)
+    y2 = tp.mlp_forward(x, sh)
+    torch.cuda.synchronize()
+    ok &= bool(torch.allclose(y1.float(), y2.float(), rtol=2e-3, atol=2e-3))
+    st = ops.device_status()
+    par.close()
+    dist.barrier()
+    if rank == 0:
+        q.put((ok, st))
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_peer_allreduce_two_ranks():
+    """The one-shot all-reduce over CUDA IPC peer mappings on 2 GPUs against NCCL's."""
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    ok, st = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert ok and st == [0, 0, 0, 0]
