@@ -48,6 +48,8 @@ EXPORTS = {
     "tempo_sm100_gemm_fp16_swiglu": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "tempo_sm100_gemm_w8a16_swiglu": (
         _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "tempo_sm100_ipc_alloc": (_i, [_sz, C.POINTER(C.c_void_p)]),
+    "tempo_sm100_ipc_free": (_i, [_vp]),
     "tempo_sm100_ipc_handle": (_i, [_vp, _vp]),
     "tempo_sm100_ipc_open": (_i, [_vp, C.POINTER(C.c_void_p)]),
     "tempo_sm100_ipc_close": (_i, [_vp]),

@@ -346,6 +346,22 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
   return run_pair_swiglu(pr, current_sms(), st);
 }
 
+int tempo_sm100_ipc_alloc(size_t bytes, void** out_ptr) {
+  if (!out_ptr || bytes == 0) return cudaErrorInvalidValue;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return e;
+  }
+  *out_ptr = p;
+  return cudaSuccess;
+}
+
+int tempo_sm100_ipc_free(void* ptr) { return cudaFree(ptr); }
+
 int tempo_sm100_ipc_handle(const void* dptr, void* out_handle) {
   if (!dptr || !out_handle) return cudaErrorInvalidValue;
   cudaIpcMemHandle_t h;

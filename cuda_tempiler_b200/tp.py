@@ -131,11 +131,16 @@ class PeerAllReduce:
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.cap = -(-cap // 8) * 8
         self.ctas = ctas
-        self.recv = torch.zeros(2 * self.tp * self.cap, dtype=torch.float16, device=self.device)
-        self.flags = torch.zeros(self.tp * 32, dtype=torch.int32, device=self.device)
+        # whole allocations of their own (an IPC handle maps an allocation from its base)
+        with torch.cuda.device(self.device):
+            r, f = C.c_void_p(), C.c_void_p()
+            _lib.check(self._lib.tempo_sm100_ipc_alloc(2 * self.tp * self.cap * 2, C.byref(r)),
+                       "ipc_alloc")
+            _lib.check(self._lib.tempo_sm100_ipc_alloc(self.tp * 32 * 4, C.byref(f)), "ipc_alloc")
+        self._own = [r.value, f.value]
         hr, hf = (C.c_uint8 * 64)(), (C.c_uint8 * 64)()
-        _lib.check(self._lib.tempo_sm100_ipc_handle(self.recv.data_ptr(), hr), "ipc_handle")
-        _lib.check(self._lib.tempo_sm100_ipc_handle(self.flags.data_ptr(), hf), "ipc_handle")
+        _lib.check(self._lib.tempo_sm100_ipc_handle(r.value, hr), "ipc_handle")
+        _lib.check(self._lib.tempo_sm100_ipc_handle(f.value, hf), "ipc_handle")
         mine = torch.tensor(list(bytes(hr)) + list(bytes(hf)), dtype=torch.uint8,
                             device=self.device)
         every = [torch.empty_like(mine) for _ in range(self.tp)]
@@ -144,8 +149,8 @@ class PeerAllReduce:
         rp, fp = [], []
         for p, t in enumerate(every):
             if p == self.rank:
-                rp.append(self.recv.data_ptr())
-                fp.append(self.flags.data_ptr())
+                rp.append(r.value)
+                fp.append(f.value)
                 continue
             raw = bytes(t.cpu().tolist())
             ptrs = []
@@ -180,9 +185,17 @@ class PeerAllReduce:
         return y
 
     def close(self):
+        """Unmap the peers' buffers, then free this rank's (after a barrier, so no peer still
+        maps them)."""
+        import torch.distributed as dist
         for p in self._opened:
             self._lib.tempo_sm100_ipc_close(p)
         self._opened = []
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._own:
+            self._lib.tempo_sm100_ipc_free(p)
+        self._own = []
 
 
 def mlp_forward(x: torch.Tensor, shard: MLPShard, group=None, gemm=None, swiglu=None,

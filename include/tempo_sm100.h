@@ -134,9 +134,13 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
                                   int ldc, int quant_kind, int group_size, void* ws,
                                   size_t ws_bytes, void* stream);
 
-/* Peer memory for the tensor-parallel exchange (one process per GPU of one node): the 64-byte
- * CUDA IPC handle of a device allocation, its mapping in another process, and the unmapping. */
+/* Peer memory for the tensor-parallel exchange (one process per GPU of one node): a zeroed
+ * device allocation of its own (an IPC handle maps a whole allocation, so the buffers must not
+ * be sub-allocations of a caching allocator) and its release, the 64-byte CUDA IPC handle of
+ * such an allocation, its mapping in another process, and the unmapping. */
 #define TEMPO_SM100_IPC_HANDLE_BYTES 64
+int tempo_sm100_ipc_alloc(size_t bytes, void** out_ptr);
+int tempo_sm100_ipc_free(void* ptr);
 int tempo_sm100_ipc_handle(const void* dptr, void* out_handle);
 int tempo_sm100_ipc_open(const void* handle, void** out_ptr);
 int tempo_sm100_ipc_close(void* ptr);
