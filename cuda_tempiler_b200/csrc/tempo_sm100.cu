@@ -136,7 +136,7 @@ size_t hyper_ws(int M, int N, int K, const Hyper& h, int sms, size_t ws_cap, siz
 }
 
 cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  if (h.bn == 0) return run_gemv(pr, st);
+  if (h.bn == 0) return run_gemv(pr, st, h.group_m);
   if (h.cta_group == 2) return run_pair(pr, h, st);
   const InstEntry* e = find_inst(pr.wkind, h.bn, h.swap);
   if (!e) return cudaErrorInvalidConfiguration;

@@ -300,16 +300,30 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
                    mZ, a);
 }
 
-// Decode-sized streaming GEMV (hyperform bn == 0): M <= 16, 256 threads, R weight rows per warp.
+// Decode-sized streaming GEMV (hyperform bn == 0): M <= 16, one CTA of kGemvThreads threads
+// per R weight rows.
 template <int WQ, int MM, int R>
 cudaError_t launch_gemv(const Problem& pr, cudaStream_t st) {
-  const int rows_per_block = 8 * R;
-  const int grid = (pr.N + rows_per_block - 1) / rows_per_block;
-  return launch_ex(k_gemv_sm100<WQ, MM, R>, dim3(grid), dim3(256), 0, st, 1,
+  const int grid = (pr.N + R - 1) / R;
+  return launch_ex(k_gemv_sm100<WQ, MM, R>, dim3(grid), dim3(kGemvThreads), 0, st, 1,
                    static_cast<const __half*>(pr.A), static_cast<const uint8_t*>(pr.W),
                    static_cast<const __half*>(pr.scale), static_cast<const uint8_t*>(pr.zero),
                    static_cast<__half*>(pr.C), pr.M, pr.N, pr.K, (long long)pr.lda,
                    (long long)pr.ldw, (long long)pr.ldc, pr.group > 0 ? pr.group : 1);
+}
+
+// Rows per CTA: the widest R in {4, 2, 1} that still gives at least kGemvMinCtasPerSm CTAs
+// per SM (so the block scheduler can balance the bytes each SM streams); wider R reuses each
+// activation chunk over more weight rows.  8 and 16 activation rows keep R <= 2 so the
+// accumulators stay in registers.
+constexpr int kGemvMinCtasPerSm = 12;
+
+int gemv_rows(int N, int M, int sms) {
+  const long long want = (long long)kGemvMinCtasPerSm * (sms > 0 ? sms : 148);
+  const int rmax = M > 4 ? 2 : 4;
+  for (int r = rmax; r > 1; r >>= 1)
+    if ((long long)N / r >= want) return r;
+  return 1;
 }
 
 template <int WQ, int R>
@@ -317,20 +331,78 @@ cudaError_t gemv_by_m(const Problem& pr, cudaStream_t st) {
   if (pr.M == 1) return launch_gemv<WQ, 1, R>(pr, st);
   if (pr.M == 2) return launch_gemv<WQ, 2, R>(pr, st);
   if (pr.M <= 4) return launch_gemv<WQ, 4, R>(pr, st);
-  // 8 and 16 activation rows: two weight rows per warp keep the accumulators in registers
-  if (pr.M <= 8) return launch_gemv<WQ, 8, 2>(pr, st);
-  return launch_gemv<WQ, 16, 2>(pr, st);
+  if (R <= 2) {
+    if (pr.M <= 8) return launch_gemv<WQ, 8, (R <= 2 ? R : 2)>(pr, st);
+    return launch_gemv<WQ, 16, (R <= 2 ? R : 2)>(pr, st);
+  }
+  return cudaErrorInvalidConfiguration;
+}
+
+template <int WQ>
+cudaError_t gemv_by_rows(const Problem& pr, int rows, cudaStream_t st) {
+  if (rows == 4) return gemv_by_m<WQ, 4>(pr, st);
+  if (rows == 2) return gemv_by_m<WQ, 2>(pr, st);
+  return gemv_by_m<WQ, 1>(pr, st);
+}
+
+// The tensor-core decode GEMV (k_gemv_mma_sm100): 16 weight rows per CTA, k split over a
+// cluster of `splits` CTAs -- the smallest power of two (at most 8) that gives every SM at
+// least kGemvMmaMinCtasPerSm CTAs.
+constexpr int kGemvMmaMinCtasPerSm = 8;
+
+int gemv_mma_splits(int N, int K, int wkind, int sms) {
+  const long long groups = (N + 15) / 16;
+  const long long want = (long long)kGemvMmaMinCtasPerSm * (sms > 0 ? sms : 148);
+  const int nch = K / (wkind == 0 ? 8 : 16);
+  int s = 1;
+  while (s < kGemvMmaMaxSplit && groups * s < want && nch / (2 * s) >= 16) s *= 2;
+  return s;
+}
+
+template <int WQ, int MG>
+cudaError_t launch_gemv_mma(const Problem& pr, int splits, cudaStream_t st) {
+  const int grid = ((pr.N + 15) / 16) * splits;
+  return launch_ex(k_gemv_mma_sm100<WQ, MG>, dim3(grid), dim3(kGemvThreads), 0, st, splits,
+                   static_cast<const __half*>(pr.A), static_cast<const uint8_t*>(pr.W),
+                   static_cast<const __half*>(pr.scale), static_cast<const uint8_t*>(pr.zero),
+                   static_cast<__half*>(pr.C), pr.M, pr.N, pr.K, (long long)pr.lda,
+                   (long long)pr.ldw, (long long)pr.ldc, pr.group > 0 ? pr.group : 1, splits);
+}
+
+template <int WQ>
+cudaError_t gemv_mma_by_m(const Problem& pr, int splits, cudaStream_t st) {
+  if (pr.M <= 8) return launch_gemv_mma<WQ, 1>(pr, splits, st);
+  return launch_gemv_mma<WQ, 2>(pr, splits, st);
 }
 
 constexpr int kGemvMaxM = 16;
+// Activation rows from which the tensor-core GEMV takes over from the CUDA-core one (measured
+// on the BASELINE shapes: fp16 weights from 5 rows, 8-bit weights -- whose CUDA-core dequant
+// adds to the FMA issue -- from 3).
+int gemv_mma_min_m(int wkind) { return wkind == 0 ? 5 : 3; }
 
-cudaError_t run_gemv(const Problem& pr, cudaStream_t st) {
+// variant (a GEMV hyperform's group_m): 1 = CUDA-core, 2 = tensor-core, anything else by M
+// (CUDA-core below gemv_mma_min_m, tensor-core from it).
+cudaError_t run_gemv(const Problem& pr, cudaStream_t st, int variant = 0) {
   if (pr.M < 1 || pr.M > kGemvMaxM) return cudaErrorInvalidConfiguration;
-  const bool wide = pr.N >= 9472;  // enough rows for 4 per warp over two waves of 148 SMs
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = dev_info(dev).sms;
+  const bool mma = variant == 2 || (variant != 1 && pr.M >= gemv_mma_min_m(pr.wkind));
+  if (mma) {
+    const int splits = gemv_mma_splits(pr.N, pr.K, pr.wkind, sms);
+    switch (pr.wkind) {
+      case 0: return gemv_mma_by_m<0>(pr, splits, st);
+      case 1: return gemv_mma_by_m<1>(pr, splits, st);
+      case 2: return gemv_mma_by_m<2>(pr, splits, st);
+      default: return cudaErrorInvalidConfiguration;
+    }
+  }
+  const int rows = gemv_rows(pr.N, pr.M, sms);
   switch (pr.wkind) {
-    case 0: return wide ? gemv_by_m<0, 4>(pr, st) : gemv_by_m<0, 2>(pr, st);
-    case 1: return wide ? gemv_by_m<1, 4>(pr, st) : gemv_by_m<1, 2>(pr, st);
-    case 2: return wide ? gemv_by_m<2, 4>(pr, st) : gemv_by_m<2, 2>(pr, st);
+    case 0: return gemv_by_rows<0>(pr, rows, st);
+    case 1: return gemv_by_rows<1>(pr, rows, st);
+    case 2: return gemv_by_rows<2>(pr, rows, st);
     default: return cudaErrorInvalidConfiguration;
   }
 }

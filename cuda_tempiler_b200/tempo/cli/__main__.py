@@ -227,6 +227,13 @@ def cmd_ship(a):
             measured = [{"kind": r["kind"], "name": r.get("name"), "M": r["M"], "N": r["N"],
                          "K": r["K"], "best": r["best"], "dispatch": r["dispatch"]}
                         for r in rows if r["kind"] in kinds]
+            if getattr(a, "merge", False) and os.path.exists(prev):
+                m0 = json.load(open(prev))
+                old = [(r["m_max"], r["bn"], r["swap"], r["group_m"], r.get("cta_group", 1))
+                       for r in m0["ladder"]]
+                lad, keep_from = ship.merge_ladder(lad, old, [r["M"] for r in rows
+                                                              if r["kind"] in kinds])
+                measured += [r for r in m0.get("rows", []) if r["M"] > keep_from]
         elif os.path.exists(prev):  # re-freeze the skeleton under the ladder already shipped
             m0 = json.load(open(prev))
             lad = [(r["m_max"], r["bn"], r["swap"], r["group_m"], r.get("cta_group", 1))
@@ -286,6 +293,9 @@ def main(argv=None):
     s = sub.add_parser("ship")
     s.add_argument("--from", dest="source", default=None)
     s.add_argument("--out", default=None)
+    s.add_argument("--merge", action="store_true",
+                   help="re-derive only the M bands the tune rows cover; keep the shipped "
+                        "ladder rows (and measured rows) above them")
     s.set_defaults(fn=cmd_ship)
     a = ap.parse_args(argv)
     return a.fn(a)

@@ -879,10 +879,18 @@ namespace tempo_sm100 {
 // At M <= 16 a 128 x N x 16 UMMA costs about as much as a wide one, so the tensor-core path is
 // instruction-bound there; this kernel instead streams each weight row once with 16-byte
 // read-only loads (kept out of L1), dequantises in registers and multiplies on the CUDA cores.
-// Warp w owns R consecutive weight rows; lane l reads 16-byte chunks l, l + 32, ... of each row.
-// Products of one 16-byte chunk are summed in packed fp16 (4 or 8 terms per half), then added
-// to fp32 accumulators; a warp shuffle reduction finishes each (m, row).
+//
+// Work split: CTA b (kGemvThreads threads) owns the R weight rows [b R, b R + R) and its threads
+// split K: thread t reads 16-byte chunks t, t + T, ... of each of the R rows, U chunks of every
+// row in flight before any of them is used.  Many small CTAs (N / R of them, thousands at the
+// BASELINE shapes) let the block scheduler even out the bytes each SM streams, where one warp
+// per row group left a ragged last wave (e.g. 240 CTAs of 16 rows on 148 SMs).  Products of
+// one chunk are summed in packed fp16 (4 or 8 terms per half), then added to fp32
+// accumulators; a warp shuffle and a fixed-order sum over the CTA's warps in shared memory
+// finish each (m, row), so results do not depend on scheduling.
 // ---------------------------------------------------------------------------------------------
+constexpr int kGemvThreads = 128;
+
 template <int WQ>
 __device__ __forceinline__ void gemv_weights(uint4 x, __half2 (&w)[8], __half2 zb, __half2 s2) {
   if (WQ == kWInt8PerChannel) {
@@ -947,37 +955,41 @@ __global__ void __launch_bounds__(256)
 }
 
 template <int WQ, int MM, int R>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kGemvThreads)
     k_gemv_sm100(const __half* __restrict__ A, const uint8_t* __restrict__ W,
                  const __half* __restrict__ scale, const uint8_t* __restrict__ zero,
                  __half* __restrict__ C, int M, int N, int K, long long lda, long long ldw,
                  long long ldc, int group) {
+  constexpr int T = kGemvThreads;
+  constexpr int NWARP = T / 32;
   constexpr int ESZ = WQ ? 1 : 2;       // weight bytes per element
   constexpr int KC = 16 / ESZ;          // k per 16-byte chunk
   constexpr int NW = KC / 2;            // packed fp16 pairs per chunk
-  const int lane = threadIdx.x & 31;
-  const int warp_g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int n0 = warp_g * R;
-  if (n0 >= N) return;
+  // chunks of each row in flight per thread: 8 / R, halved where 4+ activation rows hold the
+  // registers (keeps every instantiation free of spills)
+  constexpr int UC = MM >= 4 ? 4 : 8;
+  constexpr int U = R >= UC ? 1 : UC / R;
+  __shared__ float red[NWARP][MM * R];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int n0 = blockIdx.x * R;
   pdl_wait();
   pdl_launch_dependents();
   const int nchunks = K / KC;           // K % KC == 0 (checked by applicability)
+  const uint8_t* wrow[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) wrow[r] = W + (long long)min(n0 + r, N - 1) * ldw * ESZ;
   float acc[MM][R];
 #pragma unroll
   for (int m = 0; m < MM; ++m)
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[m][r] = 0.f;
   const int G = WQ == kWUint8Group ? group : 1;
-#pragma unroll 2
-  for (int c = lane; c < nchunks; c += 32) {
+
+  // one chunk (c) of the R rows, already loaded: dequantise, multiply, accumulate
+  auto use_chunk = [&](int c, const uint4 (&x)[R]) {
     const int k0 = c * KC;
-    uint4 x[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int n = min(n0 + r, N - 1);
-      x[r] = ld_stream(W + (long long)n * ldw * ESZ + (long long)c * 16);
-    }
-    // this chunk's weights of the R rows as packed fp16 pairs
     __half2 w[R][8];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -989,6 +1001,8 @@ __global__ void __launch_bounds__(256)
       } else {
         __half2 zb = __float2half2_rn(0.f), s2 = zb;
         if (WQ == kWUint8Group) {
+          // (measured: fetching these with the weight chunks instead costs this kernel 3-5 %
+          // at the M <= 2 it serves -- more registers, fewer resident CTAs)
           const int n = min(n0 + r, N - 1);
           const long long gi = (long long)(k0 / G) * N + n;
           zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | __ldg(zero + gi))));
@@ -1026,7 +1040,26 @@ __global__ void __launch_bounds__(256)
         acc[m][r] += f.x + f.y;
       }
     }
+  };
+
+  int c = tid;
+  // U chunks of every row issued before the first is used: U * R * 16 bytes in flight
+  for (; c + (U - 1) * T < nchunks; c += U * T) {
+    uint4 x[U][R];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int r = 0; r < R; ++r) x[u][r] = ld_stream(wrow[r] + (long long)(c + u * T) * 16);
+#pragma unroll
+    for (int u = 0; u < U; ++u) use_chunk(c + u * T, x[u]);
   }
+  for (; c < nchunks; c += T) {
+    uint4 x[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) x[r] = ld_stream(wrow[r] + (long long)c * 16);
+    use_chunk(c, x);
+  }
+
 #pragma unroll
   for (int m = 0; m < MM; ++m)
 #pragma unroll
@@ -1034,17 +1067,233 @@ __global__ void __launch_bounds__(256)
       float v = acc[m][r];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[m][r] = v;
+      if (lane == 0) red[warp][m * R + r] = v;
     }
-  if (lane == 0) {
+  __syncthreads();
+  for (int i = tid; i < MM * R; i += T) {
+    const int m = i / R;
+    const int n = n0 + (i - m * R);
+    if (m >= M || n >= N) continue;
+    float v = red[0][i];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int n = n0 + r;
-      if (n >= N) break;
+    for (int w = 1; w < NWARP; ++w) v += red[w][i];
+    const float sc = WQ == kWInt8PerChannel ? __half2float(__ldg(scale + n)) : 1.f;
+    C[(long long)m * ldc + n] = __float2half_rn(v * sc);
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// k_gemv_mma_sm100: the decode GEMV for 5..16 activation rows, with the products on the warp
+// tensor-core instruction (mma.sync m16n8k16, fp16 inputs, fp32 accumulate) instead of packed
+// fp16 FMAs.  The op is HBM-bound at these M; what limits the CUDA-core kernel above is
+// instruction issue (8 FMA instructions per activation row per 16 weights), which one MMA per
+// 16 x 8 x 16 block removes.  Operands go straight from registers (the weight chunks streamed
+// from HBM and dequantised in registers, the activation chunks from L1) -- no shared-memory
+// staging, so the 5th-generation tcgen05 path (which needs operands in shared memory / TMEM and
+// a single-thread issue chain per CTA) buys nothing here.
+//
+// Work split: a CTA (4 warps) owns 16 weight rows and one of `splits` k-slices; the k-slices of
+// a row group run in one cluster (splits CTAs) and reduce through distributed shared memory.
+// Lane (g, t) = (lane / 4, lane % 4) of warp w streams 16-byte chunk c = c0 + 16 i + 4 w + t of
+// weight rows g and g + 8; every lane with the same t holds the same k range, so mapping the
+// chunk's k values onto MMA k slots (slot 2t <-> k 4j, 2t+1 <-> 4j+1, 2t+8 <-> 4j+2, 2t+9 <->
+// 4j+3 of chunk j-th quarter) is the same permutation for the weight (A) and activation (B)
+// fragments, and the dot products are unchanged.  The CTA's four warps sum in shared memory,
+// the cluster's CTAs into rank 0, each in a fixed order (deterministic).
+// ---------------------------------------------------------------------------------------------
+constexpr int kGemvMmaMaxSplit = 8;
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int WQ, int MG>  // MG: groups of 8 activation rows (1: M <= 8, 2: M <= 16)
+__global__ void __launch_bounds__(kGemvThreads)
+    k_gemv_mma_sm100(const __half* __restrict__ A, const uint8_t* __restrict__ W,
+                     const __half* __restrict__ scale, const uint8_t* __restrict__ zero,
+                     __half* __restrict__ C, int M, int N, int K, long long lda, long long ldw,
+                     long long ldc, int group, int splits) {
+  constexpr int NWARP = kGemvThreads / 32;
+  constexpr int ESZ = WQ ? 1 : 2;   // weight bytes per element
+  constexpr int KC = 16 / ESZ;      // k per 16-byte chunk
+  constexpr int NMMA = KC / 4;      // MMAs per chunk (4 k of each lane per MMA)
+  constexpr int U = MG == 1 ? 4 : 3; // chunk steps in flight per lane (fewer where 16 rows
+                                    // of activations hold registers: no spills)
+  constexpr int TILE = 16 * 16;     // [16 weight rows][16 activation rows] fp32
+  __shared__ float red[NWARP][TILE];
+  __shared__ float slots[kGemvMmaMaxSplit][TILE];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int rgroup = blockIdx.x / splits;
+  const int rank = blockIdx.x - rgroup * splits;  // == rank in the cluster (cluster dims splits)
+  const int n0 = rgroup * 16;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int ra = min(n0 + g, N - 1), rb = min(n0 + g + 8, N - 1);
+  const uint8_t* wa = W + (long long)ra * ldw * ESZ;
+  const uint8_t* wb = W + (long long)rb * ldw * ESZ;
+  const int nch = K / KC;
+  const int c0 = (int)((long long)nch * rank / splits);
+  const int c1 = (int)((long long)nch * (rank + 1) / splits);
+  const int steps = (c1 - c0 + 15) / 16;  // warp-uniform: every lane runs every step
+  const int G = WQ == kWUint8Group ? group : 1;
+  float acc[MG][4];
+#pragma unroll
+  for (int i = 0; i < MG; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  // group-wise scale and zero-point bytes of rows ra / rb for chunk c, fetched together with
+  // the weight chunk so that their latency overlaps the HBM stream
+  struct GroupQ {
+    unsigned short sa, sb;
+    uint8_t za, zb;
+  };
+  auto load_q = [&](int c, GroupQ& q) {
+    if (WQ == kWUint8Group) {
+      const long long gi = (long long)((c * KC) / G) * N;
+      q.sa = __ldg(reinterpret_cast<const unsigned short*>(scale) + gi + ra);
+      q.sb = __ldg(reinterpret_cast<const unsigned short*>(scale) + gi + rb);
+      q.za = __ldg(zero + gi + ra);
+      q.zb = __ldg(zero + gi + rb);
+    }
+  };
+
+  auto use_chunk = [&](int c, bool valid, uint4 xa, uint4 xb, const GroupQ& q) {
+    const int k0 = c * KC;
+    __half2 ha[8], hb[8];
+    if (WQ == kWFp16) {
+      ha[0] = *reinterpret_cast<const __half2*>(&xa.x);
+      ha[1] = *reinterpret_cast<const __half2*>(&xa.y);
+      ha[2] = *reinterpret_cast<const __half2*>(&xa.z);
+      ha[3] = *reinterpret_cast<const __half2*>(&xa.w);
+      hb[0] = *reinterpret_cast<const __half2*>(&xb.x);
+      hb[1] = *reinterpret_cast<const __half2*>(&xb.y);
+      hb[2] = *reinterpret_cast<const __half2*>(&xb.z);
+      hb[3] = *reinterpret_cast<const __half2*>(&xb.w);
+    } else {
+      __half2 za = __float2half2_rn(0.f), sa = za, zb2 = za, sb = za;
+      if (WQ == kWUint8Group) {
+        za = __half2half2(__ushort_as_half((unsigned short)(0x6400u | q.za)));
+        sa = __half2half2(__ushort_as_half(q.sa));
+        zb2 = __half2half2(__ushort_as_half((unsigned short)(0x6400u | q.zb)));
+        sb = __half2half2(__ushort_as_half(q.sb));
+      }
+      gemv_weights<WQ>(xa, ha, za, sa);
+      gemv_weights<WQ>(xb, hb, zb2, sb);
+    }
+#pragma unroll
+    for (int mg = 0; mg < MG; ++mg) {
+      const int m = mg * 8 + g;
+      uint32_t bf[KC / 2];  // activation pairs of row m over the chunk's k range
+      if (valid && m < M) {
+        const uint4* ap = reinterpret_cast<const uint4*>(A + (long long)m * lda + k0);
+#pragma unroll
+        for (int q = 0; q < KC / 8; ++q) {
+          const uint4 v = __ldg(ap + q);
+          bf[4 * q + 0] = v.x;
+          bf[4 * q + 1] = v.y;
+          bf[4 * q + 2] = v.z;
+          bf[4 * q + 3] = v.w;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < KC / 2; ++q) bf[q] = 0u;  // zero activations: the chunk adds 0
+      }
+#pragma unroll
+      for (int j = 0; j < NMMA; ++j)
+        mma_16816(acc[mg], *reinterpret_cast<const uint32_t*>(&ha[2 * j]),
+                  *reinterpret_cast<const uint32_t*>(&hb[2 * j]),
+                  *reinterpret_cast<const uint32_t*>(&ha[2 * j + 1]),
+                  *reinterpret_cast<const uint32_t*>(&hb[2 * j + 1]), bf[2 * j], bf[2 * j + 1]);
+    }
+  };
+
+  const int cl = c0 + 4 * warp + t;  // this lane's chunk at step 0
+  int st = 0;
+  for (; st + U <= steps; st += U) {
+    uint4 xa[U], xb[U];
+    GroupQ q[U];
+    bool ok[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = cl + 16 * (st + u);
+      ok[u] = c < c1;
+      xa[u] = xb[u] = make_uint4(0u, 0u, 0u, 0u);
+      q[u] = GroupQ{0, 0, 0, 0};
+      if (ok[u]) {
+        xa[u] = ld_stream(wa + (long long)c * 16);
+        xb[u] = ld_stream(wb + (long long)c * 16);
+        load_q(c, q[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) use_chunk(cl + 16 * (st + u), ok[u], xa[u], xb[u], q[u]);
+  }
+  for (; st < steps; ++st) {
+    const int c = cl + 16 * st;
+    const bool ok = c < c1;
+    uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+    GroupQ q{0, 0, 0, 0};
+    if (ok) {
+      xa = ld_stream(wa + (long long)c * 16);
+      xb = ld_stream(wb + (long long)c * 16);
+      load_q(c, q);
+    }
+    use_chunk(c, ok, xa, xb, q);
+  }
+
+  // accumulator (g, 2t / 2t+1) and (g + 8, 2t / 2t+1) of each 8-row group -> [row][m]
+#pragma unroll
+  for (int mg = 0; mg < MG; ++mg) {
+    const int m = mg * 8 + 2 * t;
+    red[warp][g * 16 + m] = acc[mg][0];
+    red[warp][g * 16 + m + 1] = acc[mg][1];
+    red[warp][(g + 8) * 16 + m] = acc[mg][2];
+    red[warp][(g + 8) * 16 + m + 1] = acc[mg][3];
+  }
+  __syncthreads();
+  float part[TILE / kGemvThreads];
+#pragma unroll
+  for (int q = 0; q < TILE / kGemvThreads; ++q) {
+    const int i = tid + q * kGemvThreads;
+    float v = red[0][i];
+#pragma unroll
+    for (int w = 1; w < NWARP; ++w) v += red[w][i];
+    part[q] = v;
+  }
+  if (splits > 1) {
+    // every k-slice's CTA total into slot `rank` of the cluster's rank 0
+#pragma unroll
+    for (int q = 0; q < TILE / kGemvThreads; ++q) {
+      const int i = tid + q * kGemvThreads;
+      st_dsmem_f32(mapa_shared(smem_u32(&slots[rank][i]), 0), part[q]);
+    }
+    cluster_sync();
+    if (rank != 0) return;
+#pragma unroll
+    for (int q = 0; q < TILE / kGemvThreads; ++q) {
+      const int i = tid + q * kGemvThreads;
+      float v = slots[0][i];
+      for (int s2 = 1; s2 < splits; ++s2) v += slots[s2][i];
+      part[q] = v;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < TILE / kGemvThreads; ++q) {
+    const int i = tid + q * kGemvThreads;
+    const int r = i >> 4, m = i & 15;
+    const int n = n0 + r;
+    if (m < M && n < N) {
       const float sc = WQ == kWInt8PerChannel ? __half2float(__ldg(scale + n)) : 1.f;
-#pragma unroll
-      for (int m = 0; m < MM; ++m)
-        if (m < M) C[(long long)m * ldc + n] = __float2half_rn(acc[m][r] * sc);
+      C[(long long)m * ldc + n] = __float2half_rn(part[q] * sc);
     }
   }
 }

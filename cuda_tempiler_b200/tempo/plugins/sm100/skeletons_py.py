@@ -39,6 +39,41 @@ SWAP_BN = (16, 32, 64, 128)
 PREFILL_BN = (64, 128, 256)
 PAIR_BN = (256, 224, 192, 160, 128)
 GEMV_MAX_M = 16  # the streaming GEMV (bn 0) covers M <= 16 (k_gemv_sm100 MM 1, 2, 4, 8, 16)  # 2-CTA tile widths (k_gemm_sm100_pair<BN>)
+GEMV_THREADS = 128  # k_gemv_sm100: one CTA of 128 threads per `rows` weight rows (kGemvThreads)
+GEMV_MIN_CTAS_PER_SM = 12  # launch.cuh kGemvMinCtasPerSm
+
+
+GEMV_MMA_MIN_CTAS_PER_SM = 8  # launch.cuh kGemvMmaMinCtasPerSm
+GEMV_MMA_MAX_SPLIT = 8  # kGemvMmaMaxSplit: k-slices of a 16-row group on one cluster
+
+
+def gemv_mma_min_m(wq: int) -> int:
+    """From this M the dispatcher's GEMV uses the warp tensor-core variant (launch.cuh
+    gemv_mma_min_m): 5 for fp16 weights, 3 for 8-bit weights."""
+    return 5 if wq == 0 else 3
+
+
+def gemv_mma_splits(N: int, K: int, wq: int, sms: int = 148) -> int:
+    """Cluster k-split of the tensor-core GEMV, as launch.cuh gemv_mma_splits()."""
+    groups = -(-N // 16)
+    want = GEMV_MMA_MIN_CTAS_PER_SM * (sms if sms > 0 else 148)
+    nch = K // (8 if wq == 0 else 16)
+    s = 1
+    while s < GEMV_MMA_MAX_SPLIT and groups * s < want and nch // (2 * s) >= 16:
+        s *= 2
+    return s
+
+
+def gemv_rows(N: int, M: int, sms: int = 148) -> int:
+    """Weight rows per GEMV CTA, as launch.cuh gemv_rows(): the widest of 4, 2, 1 (2 at most
+    for M > 4) that leaves at least GEMV_MIN_CTAS_PER_SM CTAs per SM."""
+    want = GEMV_MIN_CTAS_PER_SM * (sms if sms > 0 else 148)
+    r = 2 if M > 4 else 4
+    while r > 1:
+        if N // r >= want:
+            return r
+        r //= 2
+    return 1
 SPLITS = (1, 2, 3, 4, 6, 8)
 
 
@@ -124,6 +159,8 @@ def check_op(op) -> int:
 
 
 def key_of(p: dict) -> str:
+    if p["bn"] == 0 and p.get("gemv") == "mma":
+        return f"gemv_mma_sm100_wq{p['weight']}_mg{p['mg']}_sp{p['splits']}"
     if p["bn"] == 0:
         return f"gemv_sm100_wq{p['weight']}_m{p['mm']}_r{p['rows']}"
     return (f"{FAMILY}_bn{p['bn']}_sw{p['swap']}_sp{p['splits']}_gm{p['group_m']}"
@@ -133,6 +170,8 @@ def key_of(p: dict) -> str:
 def entry_name(p: dict) -> str:
     if p.get("cta_group", 1) == 2:
         return f"tempo_sm100::k_gemm_sm100_pair<{p['bn']}>"
+    if p["bn"] == 0 and p.get("gemv") == "mma":
+        return f"tempo_sm100::k_gemv_mma_sm100<{p['weight']}, {p['mg']}>"
     if p["bn"] == 0:
         return f"tempo_sm100::k_gemv_sm100<{p['weight']}, {p.get('mm', 4)}, {p.get('rows', 4)}>"
     return f"tempo_sm100::k_gemm_sm100<{p['bn']}, {p['weight']}, {'true' if p['swap'] else 'false'}>"
@@ -195,7 +234,14 @@ class Sm100Skeletons:
             mm = 1 if M == 1 else 2 if M == 2 else 4 if M <= 4 else 8 if M <= 8 else 16
             p = dict(family=FAMILY, bn=0, swap=0, splits=1, group_m=0, weight=wq, stages=0,
                      cta_group=1, tmem_bufs=0, mm=mm,
-                     rows=2 if mm > 4 else (4 if N >= 9472 else 2))
+                     rows=gemv_rows(N, M, int(self.m.sms().value)))
+            if wq == 2:
+                p["group_size"] = group_size(op)
+            forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
+            # the warp tensor-core GEMV: 16 weight rows per CTA, k-slices on a cluster
+            p = dict(family=FAMILY, bn=0, swap=0, group_m=2, weight=wq, stages=0,
+                     cta_group=1, tmem_bufs=0, gemv="mma", mg=1 if M <= 8 else 2,
+                     splits=gemv_mma_splits(N, K, wq, int(self.m.sms().value)))
             if wq == 2:
                 p["group_size"] = group_size(op)
             forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
@@ -249,9 +295,13 @@ class Sm100Skeletons:
         p = h.params
         M, N, K = op.shapes["M"], op.shapes["N"], op.shapes["K"]
         sms = int(self.m.sms().value)
-        if p["bn"] == 0:  # streaming GEMV: HBM stream shared by all SMs, CUDA-core FMAs
+        if p["bn"] == 0:  # streaming GEMV: HBM stream shared by all SMs
             w_bytes = 1 if p["weight"] else 2
             hbm = (2.0 * M * K + w_bytes * N * K + 2.0 * M * N) / sms
+            if p.get("gemv") == "mma":  # warp MMAs of 16 x 8 x 16 (8 or 16 activation rows)
+                mmas = -(-N // 16) * (K / 16.0) * p["mg"] / sms
+                return [Atom(0, AtomKind.MEM_READ, "LDG.128.STREAM", {"HBM": hbm}),
+                        Atom(1, AtomKind.COMPUTE, "HMMA.16816.F32", {"FMA": mmas * 2048.0})]
             return [Atom(0, AtomKind.MEM_READ, "LDG.128.STREAM", {"HBM": hbm}),
                     Atom(1, AtomKind.COMPUTE, "HFMA2", {"FMA": 2.0 * M * N * K / sms})]
         g = problem_geometry(op, p)
@@ -302,9 +352,12 @@ class Sm100Skeletons:
         p = h.params
         c = pair_cfg(p["bn"]) if p.get("cta_group", 1) == 2 else \
             skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+        if p["bn"] == 0 and p.get("gemv") == "mma":
+            return Launch(grid_ctas=-(-op.shapes["N"] // 16) * p["splits"], threads=GEMV_THREADS,
+                          smem_bytes=0, entry=entry_name(p), min_ctas_per_sm=1)
         if p["bn"] == 0:
-            rows = 8 * p["rows"]
-            return Launch(grid_ctas=-(-op.shapes["N"] // rows), threads=256, smem_bytes=0,
+            return Launch(grid_ctas=-(-op.shapes["N"] // p["rows"]), threads=GEMV_THREADS,
+                          smem_bytes=0,
                           entry=entry_name(p), min_ctas_per_sm=1)
         g = problem_geometry(op, p)
         return Launch(grid_ctas=min(g["units"], int(self.m.sms().value)), threads=c["threads"],

@@ -106,23 +106,47 @@ def test_gptq_checkpoint_layout_end_to_end(dev):
     assert O.rel_l2(C.cpu().numpy(), ref) <= TOL
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 11, 16])
-@pytest.mark.parametrize("N,K", [(272, 512), (10240, 1024), (9472, 2064)])
-def test_streaming_gemv(dev, M, N, K):
-    """The CUDA-core streaming GEMV (hyperform bn=0, M <= 16: 1, 2, 4, 8 and 16 activation
-    rows per launch shape, ragged M inside each) for all three weight kinds."""
+@pytest.mark.parametrize("N,K", [(272, 512), (10240, 1024), (9472, 2064), (264, 1040)])
+def test_streaming_gemv(dev, M, N, K, variant):
+    """The decode GEMV (hyperform bn=0, M <= 16) for all three weight kinds, both variants
+    (group_m selects: 1 = CUDA-core FMAs, R rows per CTA; 2 = warp tensor-core MMAs, 16 rows
+    per CTA with the k-slices of a row group on a cluster), ragged M and ragged N (264 rows:
+    the last 16-row group is partly past N)."""
     from cuda_tempiler_b200 import ops
-    r1 = _pc(M, N, K, lambda A, W, s, C: ops.gemm_hyperform(A, W, bn=0, swap=False, scale=s, out=C))
-    G = 128 if K % 128 == 0 else 64 if K % 64 == 0 else 16
-    if K % 64 == 0:
+    r1 = _pc(M, N, K, lambda A, W, s, C: ops.gemm_hyperform(A, W, bn=0, swap=False, scale=s,
+                                                             group_m=variant, out=C))
+    if K % 64 == 0 and N % 16 == 0:
         r2 = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_hyperform(
-            A, W, bn=0, swap=False, scale=s, zero=z, group_size=G, out=C), G=128 if K % 128 == 0 else 64)
+            A, W, bn=0, swap=False, scale=s, zero=z, group_size=G, group_m=variant, out=C),
+            G=128 if K % 128 == 0 else 64)
         assert r2 <= TOL, r2
     a, b = O.inputs_layer(M, N, K, seed=M)
-    C = ops.gemm_hyperform(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), bn=0, swap=False)
+    C = ops.gemm_hyperform(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda(), bn=0,
+                           swap=False, group_m=variant)
     torch.cuda.synchronize()
     r3 = O.rel_l2(C.cpu().numpy(), O.gemm_fp16_ref(a, b))
     assert r1 <= TOL and r3 <= TOL, (r1, r3)
+    assert ops.device_status() == [0, 0, 0, 0]
+
+
+def test_gemv_variants_agree_and_repeat(dev):
+    """Both GEMV variants on the same inputs: each deterministic over repeated launches (fixed
+    reduction order, cluster k-split included), and the two within the gate of each other."""
+    from cuda_tempiler_b200 import ops
+    a, q, s = O.inputs_w8_per_channel(12, 3840, 15360, 4)
+    A, Q, S = (torch.from_numpy(x).cuda() for x in (a, q, s))
+    outs = {}
+    for v in (1, 2):
+        c1 = ops.gemm_hyperform(A, Q, bn=0, swap=False, scale=S, group_m=v)
+        c2 = ops.gemm_hyperform(A, Q, bn=0, swap=False, scale=S, group_m=v)
+        torch.cuda.synchronize()
+        assert torch.equal(c1, c2), f"variant {v} not deterministic"
+        outs[v] = c1.float().cpu().numpy()
+    assert O.rel_l2(outs[2], outs[1]) <= TOL
+    ref = O.gemm_w_ref(a, O.dequant_per_channel(q, s))
+    assert O.rel_l2(outs[2], ref) <= TOL
 
 
 @pytest.mark.parametrize("M,N,K", [(512, 1040, 2048), (1000, 2064, 1024), (2048, 5120, 5120)])

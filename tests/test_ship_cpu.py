@@ -51,7 +51,8 @@ def test_frozen_kernel_equals_skeleton(op):
 def test_select_predicate_and_fallback():
     s16, s8 = load_select("gemm_fp16"), load_select("gemm_w8a16")
     assert s16.select("gemm_fp16", 1, 4096, 3840)["bn"] == 0           # streaming GEMV
-    assert s16.select("gemm_fp16", 8, 4096, 3840)["swap"] == 1
+    assert s16.select("gemm_fp16", 8, 4096, 3840)["bn"] == 0           # GEMV (tensor-core)
+    assert s16.select("gemm_fp16", 16, 4096, 3840)["swap"] == 1
     assert s16.select("gemm_fp16", 4096, 15360, 3840)["bn"] == 256
     assert s16.select("gemm_fp16", 4, 4095, 3840) is None        # N % 8: not covered -> fallback
     assert s16.select("gemm_fp16", 4, 4096, 3840, arch="sm_70") is None
@@ -74,3 +75,19 @@ def test_library_ladder_agrees_with_select_on_cpu():
             assert out[0] >= s["bn"] and (out[1], out[3]) == (s["swap"], s["group_m"]), M
         else:
             assert (out[0], out[1], out[3]) == (s["bn"], s["swap"], s["group_m"]), M
+
+
+def test_merge_ladder_partial_retune():
+    """A tune that covers M <= 16 re-derives the bands up to 16 and keeps the shipped rows
+    above; neighbouring rows with the same choice collapse; the last row reaches INF."""
+    from cuda_tempiler_b200.tempo.plugins.sm100 import ship
+    INF = ship.INF
+    old = [(2, 0, 0, 0, 1), (16, 16, 1, 8, 1), (32, 64, 1, 8, 1), (64, 128, 1, 8, 1),
+           (256, 128, 0, 16, 1), (INF, 256, 0, 16, 2)]
+    lad, top = ship.merge_ladder([(4, 0, 0, 0, 1), (INF, 16, 1, 8, 1)], old, [1, 2, 4, 8, 16])
+    assert top == 16
+    assert lad == [(4, 0, 0, 0, 1), (16, 16, 1, 8, 1), (32, 64, 1, 8, 1), (64, 128, 1, 8, 1),
+                   (256, 128, 0, 16, 1), (INF, 256, 0, 16, 2)]
+    lad, top = ship.merge_ladder([(INF, 0, 0, 0, 1)], old, [1, 3])
+    assert top == 4 and lad[0] == (4, 0, 0, 0, 1) and lad[1] == (16, 16, 1, 8, 1)
+    assert ship.merge_ladder([], old, [1])[0] == old
