@@ -17,6 +17,9 @@ Weights N(0, 0.02), activations N(0, 1), seeded synthetic (no checkpoints).
              roofline, x cuBLAS (torch.mm timed the same way) and x naive INPUT (M <= 128);
              in_step_us is the in-step event window.
   x_cublas_step  cuBLAS time for the whole step (the same 20 GEMMs queued) / ours.
+  w8a16      (N = 1) BASELINE configs 3 and 4, every shape x M through tempo_sm100_gemm_w8a16,
+             each gated (relL2 <= 3e-3) and timed like per_gemm against cuBLAS on the weights
+             pre-dequantised to fp16 (x_cublas_fp16w; medians per config beside).
   cpu_baseline  fp32 numpy matmul (the reference's CPU path) on a bounded sample, rank 0.
 
 L2: every step streams 448 MB of distinct weights and consecutive GEMMs use different weight
@@ -54,6 +57,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-bars", action="store_true", help="skip cuBLAS/naive/CPU side measurements")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel MLP section")
+    ap.add_argument("--no-w8", action="store_true", help="skip the W8A16 (configs 3-4) section")
     ap.add_argument("--case", default=None,
                     help="profiling case NAME:M[:kind] (e.g. gate_up:4096, gate_up:1:w8pc): launch "
                          "that one GEMM warmup+steps times and print its event timing")
@@ -304,6 +308,108 @@ def tp_mlp_block(dev, world, rank, barrier):
     return rows
 
 
+# ------------------------------------------------------------------------------ configs 3-4
+def loop_ms(stream, call, n_copies, reps=24):
+    """Mean device ms of `reps` launches queued back to back, cycling over n_copies weight
+    copies (consecutive launches miss L2); one untimed pass over the copies first."""
+    import torch
+    for i in range(n_copies):
+        call(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for r in range(reps):
+        call(r % n_copies)
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def w8a16_block(dev, lib, stream, peaks):
+    """BASELINE configs 3 and 4 on one GPU: every shape x M of the 27B-class W8A16 set through
+    tempo_sm100_gemm_w8a16 (per-channel int8; group-wise uint8 + zero-point, group 128),
+    against cuBLAS (torch.mm) on the same weights pre-dequantised to fp16 -- the reference's
+    W8A16 bar, which reads twice the weight bytes.  Each result passes relL2 <= 3e-3 against an
+    fp32 product on the dequantised weights before it is timed."""
+    import torch
+
+    from cuda_tempiler_b200 import workloads as WL
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    sh = stream.cuda_stream
+    rows = []
+    for aux, kind, ms in (("per_channel", 1, WL.W8_PER_CHANNEL_M), ("group", 2, WL.W8_GROUP_M)):
+        G = WL.W8_GROUP_SIZE if kind == 2 else 0
+        for s in WL.LAYER_W8:
+            N, K = s.N, s.K
+            if kind == 1:
+                W = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+                sc = (torch.rand(N, generator=g, device=dev) * 2e-4 + 5e-5).half()
+                z = None
+                Wf = W.float() * sc.float()[:, None]
+            else:
+                W = torch.randint(0, 256, (N, K), generator=g, device=dev, dtype=torch.uint8)
+                sc = (torch.rand(K // G, N, generator=g, device=dev) * 0.019 + 1e-3).half()
+                z = torch.randint(100, 157, (K // G, N), generator=g, device=dev, dtype=torch.uint8)
+                Wf = (W.float() - z.float().repeat_interleave(G, 0).t()) * \
+                    sc.float().repeat_interleave(G, 0).t()
+            Wh = Wf.half()
+            ncp = min(8, max(2, -(-2 * 126 * 2**20 // (N * K))))
+            Ws = [W] + [W.clone() for _ in range(ncp - 1)]
+            nch = min(ncp, 4)
+            Whs = [Wh] + [Wh.clone() for _ in range(nch - 1)]
+            for M in ms:
+                A = torch.randn(M, K, generator=g, device=dev).half()
+                C = torch.empty(M, N, dtype=torch.float16, device=dev)
+                Cb = torch.empty_like(C)
+                wsb = lib.tempo_sm100_workspace_bytes(M, N, K, kind)
+                wsm = torch.zeros(max(wsb, 256), dtype=torch.uint8, device=dev)
+
+                def own(i, A=A, C=C, M=M, wsm=wsm):
+                    rc = lib.tempo_sm100_gemm_w8a16(
+                        A.data_ptr(), Ws[i].data_ptr(), sc.data_ptr(),
+                        z.data_ptr() if z is not None else None, C.data_ptr(), M, N, K, K, K, N,
+                        kind, G, wsm.data_ptr(), wsm.numel(), sh)
+                    if rc:
+                        raise RuntimeError(f"tempo_sm100_gemm_w8a16 rc={rc}")
+
+                own(0)
+                torch.cuda.synchronize()
+                ref = A.float() @ Wf.t()
+                rel = float(((C.float() - ref).norm() / ref.norm()).item())
+                del ref
+                if not rel <= 3e-3:
+                    raise RuntimeError(f"W8A16 {s.name} M={M} relL2 {rel} above the gate")
+                t_own = loop_ms(stream, own, ncp)
+                t_cb = loop_ms(stream, lambda i, A=A, Cb=Cb: torch.mm(A, Whs[i].t(), out=Cb), nch)
+                fl = WL.flops(M, N, K)
+                by = WL.algorithmic_bytes(M, N, K, 1, aux, G or 128)
+                t = t_own * 1e-3
+                t_floor = max(fl / (peaks["tc_sus"] * 1e12), by / (peaks["hbm"] * 1e9))
+                rows.append({
+                    "config": 3 if kind == 1 else 4, "gemm": s.name, "M": M, "N": N, "K": K,
+                    "us": round(t_own * 1e3, 2), "tflops": round(fl / t / 1e12, 1),
+                    "gbs": round(by / t / 1e9, 0),
+                    "bound": "tensor" if fl / (peaks["tc_sus"] * 1e12) >= by / (peaks["hbm"] * 1e9)
+                             else "hbm",
+                    "roofline_frac": round(t_floor / t, 3),
+                    "x_cublas_fp16w": round(t_cb / t_own, 3), "rel_l2": float("%.2e" % rel),
+                    "cfg": ops_select(kind, M, N, K, wsm.numel())})
+                del A, C, Cb, wsm
+            del Ws, Whs, W, Wf, Wh
+    torch.cuda.empty_cache()
+    summary = {}
+    for c in (3, 4):
+        xs = [r["x_cublas_fp16w"] for r in rows if r["config"] == c]
+        summary[f"config{c}_x_cublas_fp16w_median"] = statistics.median(xs) if xs else None
+    return rows, summary
+
+
+def ops_select(kind, M, N, K, ws_bytes):
+    from cuda_tempiler_b200 import ops
+    return ops.select(kind, M, N, K, ws_bytes)
+
+
 # ------------------------------------------------------------------------------ our arm
 def main():
     args = parse_args()
@@ -525,6 +631,10 @@ def main():
     # ---- tensor-parallel W8A16 MLP, tp = world size (reported beside)
     tp_rows = [] if args.no_tp else tp_mlp_block(dev, world, rank, barrier)
 
+    # ---- W8A16 GEMMs on one GPU (single-GPU runs only)
+    w8_rows, w8_summary = ([], {}) if (args.no_w8 or world > 1) else \
+        w8a16_block(dev, lib, stream, load_peaks())
+
     # ---- roofline of the dominant kernel, from its in-step event windows
     x = gemms[dom]
     fl = WL.flops(x["M"], x["N"], x["K"])
@@ -583,6 +693,8 @@ def main():
         "cpu_baseline": cpu,
         "per_gemm": per_gemm,
         "tp_mlp": tp_rows,
+        "w8a16": w8_rows,
+        **w8_summary,
         "x_cublas_median": statistics.median(p["x_cublas"] for p in per_gemm) if per_gemm and per_gemm[0]["x_cublas"] else None,
         "x_cublas_step": cublas_step_ms / ms_step if cublas_step_ms else None,
         "cublas_ms_per_step": cublas_step_ms,
