@@ -12,6 +12,7 @@
   verify --arch sm100 -M -N -K --out D build + reject spills / stack frames / missing sm_100a path
   measure --arch sm100 -M -N -K        GPU: correctness gate, then paired timing vs cuBLAS and naive
   tune [--set fp16|w8pc|w8g|all]       GPU: measured sweep of the shipped family -> JSON
+  calibrate [--device N]               GPU: probe the NOT_MEASURED channels -> tempo/calib/2 record
   ship --from TUNE.json                derive the M-ladder, write kernels/shipped/<op>/sm_100a
 
 Weights: --dtype-b fp16 (default) | int8 (per-channel scale) | uint8 (--scale group:128).
@@ -203,6 +204,19 @@ def cmd_tune(a):
     return tune.main(argv)
 
 
+def cmd_calibrate(a):
+    from .. import calibrate_stage
+    from ..plugins.sm100 import machine
+    rec = calibrate_stage.run(a.device)
+    path = calibrate_stage.write(rec, a.out or machine.CALIB_DIR)
+    for b in rec["binds"]:
+        print(f"  {b['symbol']:12s} {b['value']:.5g}  {b['note']}")
+    for k, v in rec["measured"].items():
+        print(f"  measured {k} = {v}")
+    print(f"wrote {path}")
+    return 0
+
+
 def cmd_ship(a):
     from ..plugins.sm100 import ship
     rows = json.load(open(a.source)) if a.source else []
@@ -290,6 +304,10 @@ def main(argv=None):
     s.add_argument("--rounds", type=int, default=5)
     s.add_argument("--out", default=None)
     s.set_defaults(fn=cmd_tune)
+    s = sub.add_parser("calibrate")
+    s.add_argument("--device", type=int, default=0)
+    s.add_argument("--out", default=None, help="record directory (default: the plugin's data/calib)")
+    s.set_defaults(fn=cmd_calibrate)
     s = sub.add_parser("ship")
     s.add_argument("--from", dest="source", default=None)
     s.add_argument("--out", default=None)

@@ -34,6 +34,23 @@ def _load_measured():
     return out, card
 
 
+CALIB_DIR = os.path.join(_HERE, "data", "calib")
+
+
+def _apply_calibration(table):
+    """Measured channel rates from the ``calibrate`` stage (tempo/calib/2 records under
+    data/calib/) replace NOT_MEASURED / UPPER_BOUND entries.  Inside the reference's tree,
+    whose calibration loader has another interface, the plugin keeps its own table."""
+    try:
+        from ...core.calib.load import apply, load_dir
+    except ImportError:
+        return table, []
+    if not os.path.isdir(CALIB_DIR):
+        return table, []
+    recs = load_dir(CALIB_DIR, ARCH)
+    return apply(table, recs, ARCH), [r["id"] for r in recs]
+
+
 class Sm100Machine:
     SMS = 148
     SCHEDULERS = 4
@@ -82,6 +99,7 @@ class Sm100Machine:
             "LAT.UMMA_128x256x16": not_measured("LAT.UMMA_128x256x16", "cycle"),
         }
         t.update(self._measured)
+        t, self.calibration = _apply_calibration(t)
         self._table = t
         self._channels = {
             "UMMA": Channel("UMMA", "sched", t["CAP.UMMA"]),

@@ -185,6 +185,30 @@ int tempo_sm100_device_status(int* out4, int reset);
 int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void* C, int M, int N, int K,
                                   int lda, int ldb, int ldc, void* stream);
 
+/* ---- calibration probes (the plugin's `calibrate` stage) ----------------------------------
+ * Replace the reference's measurement stand for its sm_70 channel rates (tools/probe.cu: a
+ * clock64 period around a loop doing one channel's work, one block per SM, recorded as
+ * tempo/calib records -- tempo/core/calib/schema.py:19-33).  Each runs one launch, synchronises
+ * `stream` and returns the cudaError_t; per-CTA clock64 periods go to the caller's DEVICE
+ * buffer (~0 when a bounded wait gave up).  They allocate nothing.
+ *
+ * Bulk-copy feed into shared memory: `ctas` CTAs each stream `chunks` 32 KB copies from `src`
+ * (`bytes`, >= 32 KB, 16-byte aligned), 4 in flight.  cycles_out[ctas]. */
+int tempo_sm100_probe_bulk_feed(const void* src, size_t bytes, int ctas, int chunks,
+                                unsigned long long* cycles_out, void* stream);
+/* One thread chasing `ring` (ring[i] = next index) for `steps` L1-bypassing loads;
+ * out2[0] = cycles. */
+int tempo_sm100_probe_chase(const unsigned* ring, int steps, unsigned long long* out2,
+                            void* stream);
+/* `ctas` CTAs of 4 warps converting a 16 KB int8 tile (`src`) to fp16 `iters` times, the GEMM
+ * kernels' conversion; out[2 * ctas]: cycles per CTA, then one converted value per CTA. */
+int tempo_sm100_probe_dequant(const void* src, int ctas, int iters, unsigned long long* out,
+                              void* stream);
+/* `ctas` CTAs of 4 warps storing `bytes_per_cta` (multiple of 16) with 16-byte stores into
+ * their own slices of `dst`; out[ctas]: cycles per CTA. */
+int tempo_sm100_probe_store(void* dst, size_t bytes_per_cta, int ctas, unsigned long long* out,
+                            void* stream);
+
 /* Library identification string. */
 const char* tempo_sm100_version(void);
 
