@@ -1983,6 +1983,17 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       const uint32_t t_acc = t_lane + buf * Cfg::ACC_STRIDE;
       const int q0 = tq * BN;
       const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
+      if (sg.contrib > 1 && (args.ws == nullptr || args.counters == nullptr)) {
+        // a tail without workspace is a host-side bug: report it instead of faulting
+        if (lane == 0 && atomicCAS(&g_status[0], 0, 2) == 0) {
+          g_status[1] = 16;
+          g_status[2] = blockIdx.x;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+        continue;
+      }
       if (sg.contrib > 1) {
         // Tail k-slice: this CTA's 128 x BN fp32 partial goes to slot (slice, t), laid out
         // [32-column chunk][row][32] so each thread writes and reads its row's 128 contiguous

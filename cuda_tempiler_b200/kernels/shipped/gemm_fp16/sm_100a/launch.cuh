@@ -469,6 +469,7 @@ struct PairPlan {
 };
 
 constexpr int kPairMinSlice = 4;  // fewest k-blocks in one tail k-slice
+constexpr double kPairSliceFixCycles = 20000.0;  // cost of one tail k-slice's fp32 round trip
 
 PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool split_tail,
                    size_t ws_bytes) {
@@ -482,8 +483,10 @@ PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool spli
   if (!split_tail || pl.tiles % P == 0) return pl;
   const int R = pl.tiles >= P ? pl.tiles % P : pl.tiles;
   const int full = (pl.tiles - R) / P;
-  // a k-slice's partial write and read-back: ~4000 cycles against a tile's 2 * bn per k-block
-  const double fix = 4000.0 / (pl.num_kb * 2.0 * bn);
+  // a k-slice's partial write and read-back, against a tile's 2 * bn cycles per k-block:
+  // ~20000 cycles (measured on B200: down M = 1024 with 3 slices on 18 tail tiles saves 8 %
+  // against two whole waves; on the 27B-class shapes at M = 512 every tail lost to whole waves)
+  const double fix = kPairSliceFixCycles / (pl.num_kb * 2.0 * bn);
   double best = pl.cost * 0.97;
   int best_s = 0;
   // at most 3 P tail units: 3 waves of slices, and (at bn 256) under 58 MB of partials
@@ -548,6 +551,7 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.sk_tiles = pl.sk_tiles;
   a.sk_splits = pl.sk_splits;
   if (pl.sk_splits > 0) {
+    if (!pr.ws || pr.ws_bytes < pl.ws_bytes) return cudaErrorInvalidValue;
     a.counters = static_cast<int*>(pr.ws);
     a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
   }
