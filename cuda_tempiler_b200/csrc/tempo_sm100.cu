@@ -227,7 +227,8 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
                             group_size)) {
     return cudaErrorInvalidConfiguration;
   }
-  Hyper h{bn, swap ? 1 : 0, splits < 1 ? 1 : splits, group_m < 1 ? 1 : group_m, max_ctas};
+  if (swap < 0 || swap > 2) return cudaErrorInvalidConfiguration;
+  Hyper h{bn, swap, splits < 1 ? 1 : splits, group_m < 1 ? 1 : group_m, max_ctas};
   Problem pr{weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
   return run(pr, h, static_cast<cudaStream_t>(stream));
 }

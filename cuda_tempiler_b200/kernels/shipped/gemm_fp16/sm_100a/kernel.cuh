@@ -503,13 +503,15 @@ __host__ __device__ constexpr int tmem_cols_for(int c) {
 
 constexpr int kMaxDynSmem = 232448;  // 227 KB per CTA on sm_100
 
-template <int BN_, int WQ_, bool SWAP_>
+// SMEMDQ_ (swapped 8-bit weights only): dequantise the weight tile into shared memory (the A
+// operand read by tcgen05.mma from smem, 4 dequant warps) instead of into TMEM.
+template <int BN_, int WQ_, bool SWAP_, bool SMEMDQ_ = false>
 struct SkelCfg {
   static constexpr int BM = 128, BN = BN_, BK = 64, WQ = WQ_;
   static constexpr bool SWAP = SWAP_;
   // Swapped 8-bit weights are dequantised straight into TMEM as the MMA's A operand
   // (tcgen05.mma A-from-TMEM); no fp16 copy of the weight tile ever lands in shared memory.
-  static constexpr bool TA = WQ != 0 && SWAP;
+  static constexpr bool TA = WQ != 0 && SWAP && !SMEMDQ_;
   static constexpr int WROWS = WQ ? (SWAP ? BM : BN) : 0;  // rows of the raw weight tile
   static constexpr int P_BYTES = TA ? 0 : BM * BK * 2;
   // TA stages cover KS = 128 k: one 128-byte (128B-swizzled) raw row per weight row and TMA
@@ -627,13 +629,13 @@ __device__ __forceinline__ void acc_chunk(uint32_t t_acc, int c, float (&f)[32])
   }
 }
 
-template <int BN, int WQ, bool SWAP>
-__global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
+template <int BN, int WQ, bool SWAP, bool SMEMDQ = false>
+__global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP, SMEMDQ>::THREADS, 1)
     k_gemm_sm100(const __grid_constant__ CUtensorMap mapP, const __grid_constant__ CUtensorMap mapQ,
                  const __grid_constant__ CUtensorMap mapW, const __grid_constant__ CUtensorMap mapC,
                  const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapZ,
                  const GemmArgs args) {
-  using Cfg = SkelCfg<BN, WQ, SWAP>;
+  using Cfg = SkelCfg<BN, WQ, SWAP, SMEMDQ>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -967,14 +969,21 @@ __global__ void __launch_bounds__(SkelCfg<BN, WQ, SWAP>::THREADS, 1)
 #pragma unroll 1
         for (int i = threadIdx.x - 64; i < (hi - lo) * G; i += 128) {
           const int lr = i / G, pc = (i - lr * G) * 4;
+          // all S slots' loads issued before the first add (S <= kMaxClusterSplitDev); the
+          // sum runs in rank order from zero, as before
+          float4 v[kMaxClusterSplitDev];
+#pragma unroll
+          for (int j = 0; j < kMaxClusterSplitDev; ++j)
+            if (j < S) v[j] = *reinterpret_cast<const float4*>(part + (j * rpo + lr) * PR + pc);
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-          for (int j = 0; j < S; ++j) {
-            const float4 v = *reinterpret_cast<const float4*>(part + (j * rpo + lr) * PR + pc);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+#pragma unroll
+          for (int j = 0; j < kMaxClusterSplitDev; ++j) {
+            if (j < S) {
+              acc.x += v[j].x;
+              acc.y += v[j].y;
+              acc.z += v[j].z;
+              acc.w += v[j].w;
+            }
           }
           // C row m, first of 4 C columns n: swapped [q][p] -> (q0 + pr, p0 + pc)
           const int pr = lo + lr;

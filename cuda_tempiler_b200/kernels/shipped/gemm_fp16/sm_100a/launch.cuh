@@ -206,10 +206,10 @@ size_t ws_needed(int tiles, int splits, int bn) {
 // ------------------------------------------------------------------------------------------
 // Instantiation table.
 // ------------------------------------------------------------------------------------------
-template <int BN, int WQ, bool SWAP>
+template <int BN, int WQ, bool SWAP, bool SMEMDQ = false>
 cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  using Cfg = SkelCfg<BN, WQ, SWAP>;
-  auto kern = k_gemm_sm100<BN, WQ, SWAP>;
+  using Cfg = SkelCfg<BN, WQ, SWAP, SMEMDQ>;
+  auto kern = k_gemm_sm100<BN, WQ, SWAP, SMEMDQ>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -266,10 +266,12 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   if (SWAP) {
     if (WQ == 0)
       ok &= make_map(&mP, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, 128, SW128);
-    else
+    else if (Cfg::TA)
       // one 128-byte row per weight row and request; the 128-byte swizzle keeps the dequant
       // threads' per-row reads bank-conflict free
       ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, Cfg::KS, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    else  // shared-memory dequant: 64-byte raw rows, as the non-swapped W8A16 tiles read them
+      ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
     ok &= make_map(&mQ, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, BN, SW128);
   } else {
     ok &= make_map(&mP, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, SW128);
@@ -438,19 +440,24 @@ struct InstEntry {
   int threads, smem, stages, tmem_cols;
 };
 
-#define TEMPO_INST(BN, WQ, SWAP)                                                        \
+// swap code in the table: 0 = not swapped, 1 = swapped (8-bit weights dequantised into TMEM),
+// 2 = swapped with the 8-bit weights dequantised into shared memory
+#define TEMPO_INST4(BN, WQ, SWAP, DQ, CODE)                                             \
   InstEntry {                                                                           \
-    WQ, BN, SWAP, &launch_inst<BN, WQ, SWAP>,                                           \
-        reinterpret_cast<const void*>(&k_gemm_sm100<BN, WQ, SWAP>),                     \
-        SkelCfg<BN, WQ, SWAP>::THREADS, SkelCfg<BN, WQ, SWAP>::SMEM,                    \
-        SkelCfg<BN, WQ, SWAP>::STAGES, SkelCfg<BN, WQ, SWAP>::TMEM_COLS                 \
+    WQ, BN, CODE, &launch_inst<BN, WQ, SWAP, DQ>,                                       \
+        reinterpret_cast<const void*>(&k_gemm_sm100<BN, WQ, SWAP, DQ>),                 \
+        SkelCfg<BN, WQ, SWAP, DQ>::THREADS, SkelCfg<BN, WQ, SWAP, DQ>::SMEM,            \
+        SkelCfg<BN, WQ, SWAP, DQ>::STAGES, SkelCfg<BN, WQ, SWAP, DQ>::TMEM_COLS         \
   }
+#define TEMPO_INST(BN, WQ, SWAP) TEMPO_INST4(BN, WQ, SWAP, false, SWAP ? 1 : 0)
 #define TEMPO_INST_WQ(BN, SWAP) TEMPO_INST(BN, 0, SWAP), TEMPO_INST(BN, 1, SWAP), TEMPO_INST(BN, 2, SWAP)
+#define TEMPO_INST_SDQ(BN) TEMPO_INST4(BN, 1, true, true, 2), TEMPO_INST4(BN, 2, true, true, 2)
 
 const InstEntry kInst[] = {
     TEMPO_INST_WQ(16, true),  TEMPO_INST_WQ(32, true),   TEMPO_INST_WQ(64, true),
     TEMPO_INST_WQ(128, true), TEMPO_INST_WQ(64, false),  TEMPO_INST_WQ(128, false),
     TEMPO_INST_WQ(256, false),
+    TEMPO_INST_SDQ(32),       TEMPO_INST_SDQ(64),        TEMPO_INST_SDQ(128),
 };
 
 // Work split of the 2-CTA kernel.  P clusters (one per SM pair) take whole 256 x BN tiles in
@@ -650,7 +657,7 @@ int pair_resources(int bn, int* out6) {
 
 const InstEntry* find_inst(int wkind, int bn, int swap) {
   for (const auto& e : kInst)
-    if (e.wkind == wkind && e.bn == bn && e.swap == (swap ? 1 : 0)) return &e;
+    if (e.wkind == wkind && e.bn == bn && e.swap == swap) return &e;
   return nullptr;
 }
 

@@ -103,7 +103,8 @@ def gemm_hyperform(A: torch.Tensor, W: torch.Tensor, *, bn: int, swap: bool, spl
                    zero: torch.Tensor | None = None, group_size: int = 0,
                    out: torch.Tensor | None = None) -> torch.Tensor:
     """Launch one explicit hyperform (search-space point) of the skeleton family; bn=0 is the
-    streaming GEMV (M <= 4)."""
+    decode GEMV (M <= 16), whose variant group_m selects: 1 CUDA-core FMAs, 2 warp tensor-core
+    MMAs, anything else by M as the dispatcher does."""
     lib = _lib.load()
     M, K = A.shape
     N = W.shape[0]

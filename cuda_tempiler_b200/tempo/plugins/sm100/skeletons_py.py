@@ -5,7 +5,8 @@ persistent, warp-specialised TMA -> mbarrier -> tcgen05.mma -> TMEM -> epilogue 
 an optional shared-memory dequant stage for 8-bit weights.  Axes:
 
   bn         MMA N tile (UMMA N): swap-AB {16, 32, 64, 128}; prefill {64, 128, 256}
-  swap_ab    1 = weights on the 128-row MMA side, activations on the narrow N side (decode)
+  swap_ab    1 = weights on the 128-row MMA side, activations on the narrow N side (decode);
+             2 = the same with 8-bit weights dequantised in shared memory instead of TMEM
   splits     k-split count; partials in a caller workspace, last-arriving CTA reduces
   group_m    raster group height (128-row tiles) for L2 reuse of operand tiles
   weight     0 fp16, 1 int8 per-channel (scale in the epilogue), 2 uint8 group-wise
@@ -36,6 +37,7 @@ FAMILY = "gemm_sm100"
 BM, BK = 128, 64
 MAX_DYN_SMEM = 232448
 SWAP_BN = (16, 32, 64, 128)
+SWAP_SDQ_BN = (32, 64, 128)  # swap 2 (shared-memory dequant) instantiations
 PREFILL_BN = (64, 128, 256)
 PAIR_BN = (256, 224, 192, 160, 128)
 GEMV_MAX_M = 16  # the streaming GEMV (bn 0) covers M <= 16 (k_gemv_sm100 MM 1, 2, 4, 8, 16)  # 2-CTA tile widths (k_gemm_sm100_pair<BN>)
@@ -91,12 +93,13 @@ def pair_cfg(bn: int) -> dict:
                 threads=192, tmem_cols=2 * acc_stride)
 
 
-def skel_cfg(bn: int, wq: int, swap: bool) -> dict:
-    """Python mirror of ``SkelCfg<BN, WQ, SWAP>`` in kernel.cuh (shared-memory plan);
-    bn == 0 is the streaming GEMV (no shared memory, no TMEM, 256 threads)."""
+def skel_cfg(bn: int, wq: int, swap: int) -> dict:
+    """Python mirror of ``SkelCfg<BN, WQ, SWAP, SMEMDQ>`` in kernel.cuh (shared-memory plan);
+    swap 2 = swapped with the 8-bit weights dequantised in shared memory (SMEMDQ);
+    bn == 0 is the decode GEMV (no dynamic shared memory, no TMEM, GEMV_THREADS threads)."""
     if bn == 0:
-        return dict(stage_bytes=0, stages=0, smem=0, threads=256, tmem_cols=0)
-    ta = bool(wq) and swap  # 8-bit weights dequantised into TMEM as the A operand
+        return dict(stage_bytes=0, stages=0, smem=0, threads=GEMV_THREADS, tmem_cols=0)
+    ta = bool(wq) and swap == 1  # 8-bit weights dequantised into TMEM as the A operand
     wrows = (BM if swap else bn) if wq else 0
     ks = 128 if ta else BK  # k elements per stage
     p_bytes, q_bytes, raw = (0 if ta else BM * BK * 2), bn * ks * 2, wrows * ks
@@ -174,6 +177,8 @@ def entry_name(p: dict) -> str:
         return f"tempo_sm100::k_gemv_mma_sm100<{p['weight']}, {p['mg']}>"
     if p["bn"] == 0:
         return f"tempo_sm100::k_gemv_sm100<{p['weight']}, {p.get('mm', 4)}, {p.get('rows', 4)}>"
+    if p["swap"] == 2:
+        return f"tempo_sm100::k_gemm_sm100<{p['bn']}, {p['weight']}, true, true>"
     return f"tempo_sm100::k_gemm_sm100<{p['bn']}, {p['weight']}, {'true' if p['swap'] else 'false'}>"
 
 
@@ -207,7 +212,7 @@ class Sm100Skeletons:
         tk = next((t for t in self.sync.transactions() if t.id == "gmem->smem"), None)
         if tk is None or not tk.consumes_registers:
             return 0
-        c = skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+        c = skel_cfg(p["bn"], p["weight"], int(p["swap"]))
         return (c["stages"] * c["stage_bytes"]) // (4 * c["threads"])
 
     def ops(self):
@@ -247,6 +252,8 @@ class Sm100Skeletons:
             forms_out.append(Hyperform(plugin=self.m.arch(), params=p, key=key_of(p)))
         if M <= 256:
             forms += [(bn, 1) for bn in SWAP_BN]
+            if wq:  # swapped 8-bit weights dequantised in shared memory instead of TMEM
+                forms += [(bn, 2) for bn in SWAP_SDQ_BN]
         forms += [(bn, 0) for bn in PREFILL_BN]
         if wq == 0 and M > 128:  # 2-CTA cluster tiles (cta_group::2); splits 2 = stream-K
             for bn in PAIR_BN:
@@ -260,7 +267,7 @@ class Sm100Skeletons:
                 if splits > 1 and splits > num_kb // 2:
                     continue
                 for gm in ((8,) if swap else (8, 16)):
-                    c = skel_cfg(bn, wq, bool(swap))
+                    c = skel_cfg(bn, wq, int(swap))
                     p = dict(family=FAMILY, bn=bn, swap=swap, splits=splits, group_m=gm,
                              weight=wq, stages=c["stages"], cta_group=1, tmem_bufs=2)
                     if wq == 2:
@@ -342,7 +349,7 @@ class Sm100Skeletons:
     def resources_of(self, op, h):
         p = h.params
         c = pair_cfg(p["bn"]) if p.get("cta_group", 1) == 2 else \
-            skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+            skel_cfg(p["bn"], p["weight"], int(p["swap"]))
         regs = self._facts.get(entry_name(p), {}).get("regs", 128 if p["bn"] else 64)
         if p["bn"]:
             regs += self._staging_regs(p)
@@ -351,7 +358,7 @@ class Sm100Skeletons:
     def launch_of(self, op, h):
         p = h.params
         c = pair_cfg(p["bn"]) if p.get("cta_group", 1) == 2 else \
-            skel_cfg(p["bn"], p["weight"], bool(p["swap"]))
+            skel_cfg(p["bn"], p["weight"], int(p["swap"]))
         if p["bn"] == 0 and p.get("gemv") == "mma":
             return Launch(grid_ctas=-(-op.shapes["N"] // 16) * p["splits"], threads=GEMV_THREADS,
                           smem_bytes=0, entry=entry_name(p), min_ctas_per_sm=1)

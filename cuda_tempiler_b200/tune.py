@@ -19,7 +19,7 @@ import torch
 from . import ops
 from ._lib import NotCovered
 
-HYPER = {"swap": [16, 32, 64, 128], "noswap": [64, 128, 256]}
+HYPER = {"swap": [16, 32, 64, 128], "noswap": [64, 128, 256], "swap_sdq": [32, 64, 128]}
 
 
 def model_splits(kind, M, N, K, bn, swap):
@@ -88,11 +88,14 @@ def tune_problem(kind, M, N, K, dev, flush, g, rounds=7, quick=False, kinds_bn=N
     rows = []
     cands = [(bn, True) for bn in HYPER["swap"] if M <= 256 or kind != 0] + \
         [(bn, False) for bn in HYPER["noswap"]]
+    if kind != 0:  # swapped 8-bit weights dequantised in shared memory (swap code 2)
+        cands += [(bn, 2) for bn in HYPER["swap_sdq"]]
     if M <= 16:
         cands = [(0, False)] + cands  # the streaming GEMV
     if quick:  # only the tiles that can win at this M
         cands = [(bn, sw) for bn, sw in cands
                  if bn == 0 or (sw and bn >= min(M, 128) and bn <= max(16, 2 * M))
+                 or (sw == 2 and bn >= min(M, 128) // 2 and bn <= max(32, 2 * M))
                  or (not sw and M >= 128)]
     pair = [(bn, sk) for bn in (256, 224, 192, 160, 128) for sk in (1, 2)] \
         if kind == 0 and M >= 512 else []

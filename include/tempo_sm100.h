@@ -71,7 +71,9 @@ int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, cons
 size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind);
 
 /* One explicit hyperform (the plugin's search axes; used by the build/measure stages and the
- * tuner).  bn: MMA N tile (16..256), swap: 1 = weights on the 128-row MMA side, splits: k-split
+ * tuner).  bn: MMA N tile (16..256), swap: 1 = weights on the 128-row MMA side (8-bit weights
+ * dequantised into TMEM), 2 = the same with 8-bit weights dequantised into shared memory
+ * (weight_kind 1 or 2, bn 32 / 64 / 128), splits: k-split
  * count (1 = none), group_m: raster group height in 128-row tiles, max_ctas: persistent grid
  * cap (0 = one CTA per SM).  Returns 9 if the hyperform is not instantiated or does not fit. */
 int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, const void* scale,
@@ -82,7 +84,7 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
 /* As tempo_sm100_gemm_hyperform with the cluster axis: cta_group 2 runs fp16 prefill tiles of
  * 256 x bn (bn 128 or 256) on 2-CTA clusters with tcgen05.mma.cta_group::2 (weight_kind 0,
  * swap 0).  There splits 1 = one cluster per tile; splits > 1 lets a ragged last wave run as
- * stream-K (each cluster a contiguous run of k-blocks; needs up to
+ * a split tail (its tiles cut into k-slices, reduced in k order by the last slice; needs up to
  * 65536 + 3 * P * 2 * 128 * bn * 4 bytes of workspace for P = SMs / 2 clusters, else the
  * launch stays data-parallel).  cta_group 1 is tempo_sm100_gemm_hyperform. */
 int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W, const void* scale,

@@ -53,7 +53,9 @@ def test_group_dispatch(dev, M, N, K):
     assert r <= TOL, r
 
 
-HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, False), (256, False)]
+# swap 2: swapped with the 8-bit weights dequantised in shared memory (W8A16 only)
+HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, False), (256, False),
+         (32, 2), (64, 2), (128, 2)]
 
 
 @pytest.mark.parametrize("bn,swap", HYPER)
@@ -61,6 +63,13 @@ HYPER = [(16, True), (32, True), (64, True), (128, True), (64, False), (128, Fal
 def test_every_hyperform(dev, bn, swap, splits):
     from cuda_tempiler_b200 import ops
     M = 24 if swap else 260
+    if swap == 2:
+        # shared-memory dequant: ragged M and N, splits through the cluster exchange
+        r1 = _pc(37, 528, 2048, lambda A, W, s, C: ops.gemm_hyperform(
+            A, W, bn=bn, swap=2, splits=splits, scale=s, out=C))
+        r2 = _grp(37, 528, 2048, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+            A, W, bn=bn, swap=2, splits=splits, scale=s, zero=z, group_size=G, out=C))
+        assert r1 <= TOL and r2 <= TOL, (r1, r2)
     r1 = _pc(M, 784, 1024, lambda A, W, s, C: ops.gemm_hyperform(
         A, W, bn=bn, swap=swap, splits=splits, scale=s, out=C))
     r2 = _grp(M, 784, 1024, lambda A, W, s, z, G, C: ops.gemm_hyperform(
@@ -84,6 +93,8 @@ def test_resources_match_python_plan(dev):
     lib = _lib.load()
     for wq in (0, 1, 2):
         for bn, swap in HYPER:
+            if wq == 0 and swap == 2:
+                continue  # fp16 weights need no dequant: not instantiated
             out = (C.c_int * 6)()
             assert lib.tempo_sm100_hyperform_resources(wq, bn, int(swap), out) == 0
             c = skel_cfg(bn, wq, swap)
