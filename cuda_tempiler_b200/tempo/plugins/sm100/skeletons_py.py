@@ -321,7 +321,8 @@ class Sm100Skeletons:
         bn, wq = p["bn"], p["weight"]
         flops = kb * 2.0 * BM * bn * BK
         b_rows = bn // 2 if p.get("cta_group", 1) == 2 else bn  # B rows this SM holds
-        smem_rd = kb * (BM + b_rows) * BK * 2.0
+        ta = bool(wq) and p["swap"] == 1  # A operand (weights) from TMEM, not shared memory
+        smem_rd = kb * ((0 if ta else BM) + b_rows) * BK * 2.0
         w_rows = BM if p["swap"] else bn
         act_rows = bn if p["swap"] else BM
         if p.get("cta_group", 1) == 2:
@@ -342,8 +343,9 @@ class Sm100Skeletons:
             Atom(5, AtomKind.MEM_WRITE, "EPI.TMEM_TO_GLOBAL", {"EPI": epi}, region="epilogue"),
         ]
         if wq:
+            # CAP.DEQ is measured for 4 dequant warps; the TMEM-A tiles run 8
             atoms.append(Atom(6, AtomKind.COMPUTE, "DEQUANT.U8_TO_F16",
-                              {"DEQ": kb * w_rows * BK * 1.0}, region="dequant"))
+                              {"DEQ": kb * w_rows * BK * (0.5 if ta else 1.0)}, region="dequant"))
         return atoms
 
     def resources_of(self, op, h):
