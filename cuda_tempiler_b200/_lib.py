@@ -56,6 +56,9 @@ EXPORTS = {
     "tempo_sm100_allreduce_oneshot": (
         _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
              _i, _i, C.c_uint, _i, _vp]),
+    "tempo_sm100_allreduce_oneshot_timed": (
+        _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+             _i, _i, C.c_uint, _i, C.c_ulonglong, _vp]),
     "tempo_sm100_version": (C.c_char_p, []),
     "tempo_sm100_probe_bulk_feed": (_i, [_vp, _sz, _i, _i, _vp, _vp]),
     "tempo_sm100_probe_chase": (_i, [_vp, _i, _vp, _vp]),

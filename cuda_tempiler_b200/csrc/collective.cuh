@@ -38,9 +38,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// src and dst may be the same buffer (an in-place all-reduce): neither is __restrict__.  Each
+// thread reads src[v] and later writes dst[v] only for its own v, after a __syncthreads, so
+// aliasing is safe.  wait_ns bounds the flag wait (2 s in the public entry point).
 __global__ void __launch_bounds__(256)
-    k_allreduce_oneshot(const __half* __restrict__ src, __half* __restrict__ dst, long long n,
-                        long long cap, PeerSet peers, int tp, int rank, uint32_t epoch) {
+    k_allreduce_oneshot(const __half* src, __half* dst, long long n, long long cap,
+                        const __grid_constant__ PeerSet peers, int tp, int rank, uint32_t epoch,
+                        unsigned long long wait_ns) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // src comes from the preceding GEMM
   const long long nv = n / 8;  // 16-byte vectors
   const long long per = (nv + gridDim.x - 1) / gridDim.x;
@@ -63,7 +67,7 @@ __global__ void __launch_bounds__(256)
     const uint32_t* f = peers.flags[rank] + threadIdx.x * kArMaxCtas + blockIdx.x;
     const uint64_t t0 = globaltimer();
     while (ld_acquire_sys(f) != epoch) {
-      if (globaltimer() - t0 > 2000000000ull) {
+      if (globaltimer() - t0 > wait_ns) {
         if (atomicCAS(&g_status[0], 0, 1) == 0) {
           g_status[1] = 20;  // all-reduce wait
           g_status[2] = blockIdx.x;

@@ -164,6 +164,7 @@ int tempo_sm100_gemm_fp16_applicable(const void* A, const void* B, const void* C
 int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                           int ldb, int ldc, void* ws, size_t ws_bytes, void* stream) {
   if (!fp16_applicable(A, B, C, M, N, K, lda, ldb, ldc)) return cudaErrorInvalidConfiguration;
+  if (ws && !aligned16(ws)) return cudaErrorInvalidValue;  // counters, fp32 partials
   Hyper h{};
   if (!select_hyper(0, M, N, K, ws ? ws_bytes : 0, h, current_sms()))
     return cudaErrorInvalidConfiguration;
@@ -183,6 +184,8 @@ int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, cons
                            int group_size, void* ws, size_t ws_bytes, void* stream) {
   if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, quant_kind, group_size))
     return cudaErrorInvalidConfiguration;
+  // the expanded weights are written with 16-byte stores from the start of ws
+  if (ws && !aligned16(ws)) return cudaErrorInvalidValue;
   const int sms = current_sms();
   if (M >= kExpandMinM && ws) {
     // expanded weights at the front of the workspace, the fp16 launch's workspace behind them
@@ -335,6 +338,7 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
                                   size_t ws_bytes, void* stream) {
   if (M < kExpandMinM || N % 128 || !ws || ws_bytes < expand_ws_bytes(N, K))
     return cudaErrorInvalidConfiguration;
+  if (!aligned16(ws)) return cudaErrorInvalidValue;
   if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, N, quant_kind, group_size) ||
       ldc < N / 2 || (ldc % 8))
     return cudaErrorInvalidConfiguration;
@@ -380,13 +384,15 @@ int tempo_sm100_ipc_open(const void* handle, void** out_ptr) {
 
 int tempo_sm100_ipc_close(void* ptr) { return cudaIpcCloseMemHandle(ptr); }
 
-int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,
-                                  void* const* recv, void* const* flags, int tp, int rank,
-                                  unsigned epoch, int ctas, void* stream) {
+int tempo_sm100_allreduce_oneshot_timed(const void* src, void* dst, long long n, long long cap,
+                                        void* const* recv, void* const* flags, int tp, int rank,
+                                        unsigned epoch, int ctas, unsigned long long wait_ns,
+                                        void* stream) {
   if (!src || !dst || !recv || !flags || tp < 1 || tp > kArMaxTp || rank < 0 || rank >= tp)
     return cudaErrorInvalidValue;
   if (n <= 0 || (n % 8) || n > cap || (cap % 8) || ctas < 1 || ctas > kArMaxCtas || epoch == 0)
     return cudaErrorInvalidValue;
+  if (wait_ns == 0 || wait_ns > kWaitLimitNs) return cudaErrorInvalidValue;
   if (!aligned16(src) || !aligned16(dst)) return cudaErrorInvalidValue;
   PeerSet ps{};
   for (int p = 0; p < tp; ++p) {
@@ -396,7 +402,14 @@ int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long 
   }
   return launch_ex(k_allreduce_oneshot, dim3(ctas), dim3(256), 0,
                    static_cast<cudaStream_t>(stream), 1, static_cast<const __half*>(src),
-                   static_cast<__half*>(dst), n, cap, ps, tp, rank, (uint32_t)epoch);
+                   static_cast<__half*>(dst), n, cap, ps, tp, rank, (uint32_t)epoch, wait_ns);
+}
+
+int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,
+                                  void* const* recv, void* const* flags, int tp, int rank,
+                                  unsigned epoch, int ctas, void* stream) {
+  return tempo_sm100_allreduce_oneshot_timed(src, dst, n, cap, recv, flags, tp, rank, epoch, ctas,
+                                             kWaitLimitNs, stream);
 }
 
 int tempo_sm100_device_status(int* out4, int reset) {

@@ -1,11 +1,44 @@
-"""Registry "shape -> variant -> fallback", serialisable, read by the ship dispatcher
-(reference tempo/core/emit/registry.py:39-83).  A fallback is mandatory: predicate coverage is
-never complete.  Predicate keys: ``x`` equality, ``x_max`` / ``x_min`` inclusive bounds,
-``x_divides`` (x % v == 0)."""
+"""Shape registry: an ordered list of (predicate -> kernel) entries plus a mandatory fallback,
+serialisable as a ``tempo/registry/1`` document (the reference's format,
+tempo/core/emit/registry.py:39-83).  Predicate coverage is never complete, so a registry always
+names what happens to a problem no entry matches: the caller's own path.
+
+Predicate keys are the interface's: ``x`` equality, ``x_max`` / ``x_min`` inclusive bounds,
+``x_divides`` (x % value == 0); a bound on a keyword the caller did not supply fails.  Each
+predicate is compiled once into a list of checks (``compile_predicate``).
+"""
 from __future__ import annotations
 
 import json
-from dataclasses import dataclass, field
+import operator
+from dataclasses import asdict, dataclass, field
+from typing import Callable
+
+SCHEMA = "tempo/registry/1"
+
+# suffix -> (how the keyword's value must relate to the predicate's value)
+_RELATIONS = (
+    ("_max", operator.le),
+    ("_min", operator.ge),
+    ("_divides", lambda x, v: x % v == 0),
+)
+
+
+def _check(key: str, want) -> Callable[[dict], bool]:
+    for suffix, rel in _RELATIONS:
+        if key.endswith(suffix):
+            name = key[: -len(suffix)]
+            return lambda kw: kw.get(name) is not None and bool(rel(kw[name], want))
+    return lambda kw: kw.get(key) == want
+
+
+def compile_predicate(pred: dict) -> Callable[[dict], bool]:
+    checks = [_check(k, v) for k, v in pred.items()]
+    return lambda kw: all(c(kw) for c in checks)
+
+
+def _match(pred: dict, kw: dict) -> bool:
+    return compile_predicate(pred)(kw)
 
 
 @dataclass
@@ -14,6 +47,12 @@ class Entry:
     kernel_id: str
     params: dict = field(default_factory=dict)
     note: str = ""
+
+    def __post_init__(self):
+        self._test = compile_predicate(self.predicate)
+
+    def covers(self, **kw) -> bool:
+        return self._test(kw)
 
 
 @dataclass
@@ -24,42 +63,20 @@ class Registry:
     fallback: str = "the caller's own path"
 
     def select(self, **kw):
-        for e in self.entries:
-            if _match(e.predicate, kw):
-                return e
-        return None
+        """The first entry whose predicate holds, or None (= take ``fallback``)."""
+        return next((e for e in self.entries if e.covers(**kw)), None)
 
     def to_json(self) -> str:
-        return json.dumps({"schema": "tempo/registry/1", "op": self.op, "arch": self.arch,
-                           "fallback": self.fallback,
-                           "entries": [{"predicate": e.predicate, "kernel_id": e.kernel_id,
-                                        "params": e.params, "note": e.note} for e in self.entries]},
-                          ensure_ascii=False, indent=2, sort_keys=True)
+        doc = {"schema": SCHEMA, "op": self.op, "arch": self.arch, "fallback": self.fallback,
+               "entries": [{k: v for k, v in asdict(e).items()} for e in self.entries]}
+        return json.dumps(doc, ensure_ascii=False, indent=2, sort_keys=True)
 
     @classmethod
     def from_json(cls, text: str) -> "Registry":
-        d = json.loads(text)
-        if d.get("schema") != "tempo/registry/1":
-            raise ValueError("not a tempo/registry/1 document")
-        return cls(op=d["op"], arch=d["arch"], fallback=d["fallback"],
-                   entries=[Entry(e["predicate"], e["kernel_id"], e.get("params", {}),
-                                  e.get("note", "")) for e in d["entries"]])
-
-
-def _match(pred, kw) -> bool:
-    for k, v in pred.items():
-        if k.endswith("_max"):
-            x = kw.get(k[:-4])
-            if x is None or x > v:
-                return False
-        elif k.endswith("_min"):
-            x = kw.get(k[:-4])
-            if x is None or x < v:
-                return False
-        elif k.endswith("_divides"):
-            x = kw.get(k[:-8])
-            if x is None or x % v:
-                return False
-        elif kw.get(k) != v:
-            return False
-    return True
+        doc = json.loads(text)
+        if doc.get("schema") != SCHEMA:
+            raise ValueError(f"document schema {doc.get('schema')!r} is not {SCHEMA!r}")
+        entries = [Entry(predicate=e["predicate"], kernel_id=e["kernel_id"],
+                         params=e.get("params", {}), note=e.get("note", ""))
+                   for e in doc["entries"]]
+        return cls(op=doc["op"], arch=doc["arch"], entries=entries, fallback=doc["fallback"])

@@ -1,11 +1,13 @@
 """``tempo/atoms/1`` JSON and a stable hash (insensitive to dict order) used to name ship
-directories (reference tempo/core/ir/serialize.py)."""
+directories.  The document's keys, the 6-digit rounding and the 16-hex sha256 prefix are the
+reference's format (tempo/core/ir/serialize.py), kept so that hashes name the same atoms; the
+pipeline only writes these documents, it never reads them back."""
 from __future__ import annotations
 
 import hashlib
 import json
 
-from ...plugins.base import Atom, AtomKind, Dep
+from ...plugins.base import AtomKind
 
 SCHEMA = "tempo/atoms/1"
 
@@ -20,23 +22,5 @@ def to_json(atoms, meta=None) -> str:
     return json.dumps(doc, ensure_ascii=False, sort_keys=True, indent=2)
 
 
-def from_json(text: str):
-    doc = json.loads(text)
-    if doc.get("schema") != SCHEMA:
-        raise ValueError(f"schema {doc.get('schema')!r}, expected {SCHEMA!r}")
-    return [Atom(uid=a["uid"], kind=AtomKind(a["kind"]), op_id=a["op_id"],
-                 footprint=dict(a["footprint"]), latency=a["latency"], token=a.get("token"),
-                 deps=tuple(Dep(d["src"], d["type"], d.get("distance", 0), d.get("min_gap", 0.0))
-                            for d in a.get("deps", ())),
-                 region=a.get("region", "body")) for a in doc["atoms"]]
-
-
 def stable_hash(atoms, meta=None) -> str:
     return hashlib.sha256(to_json(atoms, meta).encode("utf-8")).hexdigest()[:16]
-
-
-def diff(a, b) -> list:
-    from .atom import channel_load
-    la, lb = channel_load(a), channel_load(b)
-    return [(k, la.get(k, 0.0), lb.get(k, 0.0)) for k in sorted(set(la) | set(lb))
-            if abs(la.get(k, 0.0) - lb.get(k, 0.0)) > 1e-9]

@@ -1,14 +1,19 @@
-"""Lower bound of the period (reference tempo/core/model/bound.py:61-162):
+"""Lower bound of the period of a schedule, T >= max(ResMII, RecMII) -- the reference's
+model (tempo/core/model/bound.py:61-162), computed here as follows:
 
-    ResMII = max over channels (load / capacity),  RecMII = max mean cycle of the dependence
-    graph,  T >= max(ResMII, RecMII).
+* ResMII: each channel that carries load and has a usable capacity contributes a time; the
+  largest is ResMII and names the binding channel.  A channel of scope "sm" has a capacity in
+  units per cycle for the whole SM, and the per-warp load is multiplied by the resident warps;
+  a channel of scope "sched" has a capacity in cycles per unit of load.
+* RecMII: the maximum mean cycle of the loop-carried dependence graph (Karp, below).
 
-The bound is not a prediction.  It must be able to stay silent: when no channel with a usable
-(non-NOT_MEASURED) rate carries load, it returns ``silent=True`` instead of a wrong number.
-SPEC (datasheet) rates are refused in a time bound.
+The bound is a floor, not a prediction, and it may stay silent: when no loaded channel has a
+usable (measured or upper-bound) rate it says so instead of inventing a number.  Datasheet
+(SPEC) rates are refused outright.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 from ...plugins.base import spec_forbidden_in_time_bound
@@ -26,34 +31,46 @@ class Bound:
     silent_reason: str = ""
     uses_not_measured: tuple = ()
 
+    @classmethod
+    def without_model(cls, unmeasured: tuple) -> "Bound":
+        why = "none of the loaded channels has a usable rate"
+        if unmeasured:
+            why += " (unmeasured: " + ", ".join(unmeasured) + ")"
+        nan = math.nan
+        return cls(T=nan, res_mii=nan, rec_mii=nan, binding="", silent=True,
+                   silent_reason=why, uses_not_measured=unmeasured)
+
     def render(self) -> str:
         if self.silent:
             return "MODEL SILENT: " + self.silent_reason
-        s = (f"T >= {self.T:.2f} cycles (ResMII {self.res_mii:.2f}, RecMII {self.rec_mii:.2f}), "
-             f"bound by {self.binding}")
+        text = (f"T >= {self.T:.2f} cycles, bound by {self.binding} "
+                f"[ResMII {self.res_mii:.2f}, RecMII {self.rec_mii:.2f}]")
         if self.uses_not_measured:
-            s += "\n  WARNING: rests on unmeasured rates: " + ", ".join(self.uses_not_measured)
-        return s
+            text += "\n  caution, unmeasured rates were skipped: " + ", ".join(self.uses_not_measured)
+        return text
+
+
+_TINY = 1e-12
+# scope -> time of `load` on a channel of capacity `cap` with `warps` resident warps
+_CHANNEL_TIME = {
+    "sm": lambda load, cap, warps: load * max(1, warps) / max(cap, _TINY),
+    "sched": lambda load, cap, warps: load * cap,
+}
 
 
 def res_mii(atoms, channels, warps_per_sm: int = 1, schedulers: int = 1):
-    """scope "sm": capacity is units per cycle for the whole SM and the per-warp load scales
-    with the resident warps; scope "sched": capacity is cycles per unit of load."""
-    per, nm = {}, []
+    """(per-channel times, unmeasured rate symbols) for the channels the atoms load."""
+    times, unmeasured = {}, []
     for name, load in channel_load(atoms).items():
-        ch = channels.get(name)
-        if ch is None:
+        if name not in channels:
             continue
-        cap = ch.capacity
-        spec_forbidden_in_time_bound(cap)
-        if cap.status == "NOT_MEASURED":
-            nm.append(cap.symbol)
-            continue
-        if ch.scope == "sm":
-            per[name] = load * max(1, warps_per_sm) / max(1e-12, cap.value)
+        ch = channels[name]
+        spec_forbidden_in_time_bound(ch.capacity)
+        if ch.capacity.status == "NOT_MEASURED":
+            unmeasured.append(ch.capacity.symbol)
         else:
-            per[name] = load * cap.value
-    return per, tuple(nm)
+            times[name] = _CHANNEL_TIME[ch.scope](load, ch.capacity.value, warps_per_sm)
+    return times, tuple(unmeasured)
 
 
 def _max_mean_cycle(n, edges):
@@ -106,22 +123,19 @@ def rec_mii(atoms) -> float:
 
 
 def bound(atoms, channels, warps_per_sm: int = 1, schedulers: int = 1) -> Bound:
-    per, nm = res_mii(atoms, channels, warps_per_sm, schedulers)
-    if not per:
-        return Bound(T=float("nan"), res_mii=float("nan"), rec_mii=float("nan"), binding="",
-                     silent=True, uses_not_measured=nm,
-                     silent_reason="no channel with a usable rate carries the binding load"
-                     + (f" (not measured: {', '.join(nm)})" if nm else ""))
-    binding = max(per, key=per.get)
-    r = per[binding]
+    times, unmeasured = res_mii(atoms, channels, warps_per_sm, schedulers)
+    if not times:
+        return Bound.without_model(unmeasured)
+    res_name, res = max(times.items(), key=lambda kv: kv[1])
     rec = rec_mii(atoms)
-    return Bound(T=max(r, rec), res_mii=r, rec_mii=rec,
-                 binding=binding if r >= rec else "RECURRENCE", per_channel=per,
-                 uses_not_measured=nm)
+    return Bound(T=max(res, rec), res_mii=res, rec_mii=rec,
+                 binding="RECURRENCE" if rec > res else res_name, per_channel=times,
+                 uses_not_measured=unmeasured)
 
 
 def headroom(measured_cycles: float, b: Bound) -> float:
-    """How far above the bound a measurement sits; below 1 means a unit error."""
-    if b.silent or not b.T or b.T != b.T:
-        return float("nan")
+    """measured / bound: how far a measurement sits above the floor (NaN without a model; a
+    value below 1 means the model or the measurement has a unit error)."""
+    if b.silent or not b.T > 0:
+        return math.nan
     return measured_cycles / b.T

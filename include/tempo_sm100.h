@@ -20,8 +20,9 @@
  * its first use).  Its first 64 KiB hold arrival counters, which every launch leaves at zero;
  * the rest holds fp32 partials, which need no clearing.  Query the size with
  * tempo_sm100_workspace_bytes.  ws == NULL or too small is legal: the dispatcher then picks
- * a configuration without split-K.  One workspace must not be shared by launches that can
- * run concurrently (different streams).
+ * a configuration without split-K.  A non-NULL ws must be 16-byte aligned (else 1,
+ * cudaErrorInvalidValue, and nothing is launched).  One workspace must not be shared by
+ * launches that can run concurrently (different streams).
  *
  * Threading: all entry points are re-entrant; per-device one-time set-up is internal.
  */
@@ -158,6 +159,13 @@ int tempo_sm100_ipc_close(void* ptr);
 int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,
                                   void* const* recv, void* const* flags, int tp, int rank,
                                   unsigned epoch, int ctas, void* stream);
+/* The same with the flag wait bounded by wait_ns (1 .. 2e9 ns) instead of 2 s: a rank that
+ * has not arrived by then leaves status 1, role 20 and the output undefined.  For callers
+ * that want a faster failure report than 2 s (and for the test that makes the wait run out). */
+int tempo_sm100_allreduce_oneshot_timed(const void* src, void* dst, long long n, long long cap,
+                                        void* const* recv, void* const* flags, int tp, int rank,
+                                        unsigned epoch, int ctas, unsigned long long wait_ns,
+                                        void* stream);
 
 /* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
  * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the

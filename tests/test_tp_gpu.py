@@ -172,6 +172,38 @@ def test_allreduce_oneshot_emulated_ranks(dev):
     assert ops_status() == [0, 0, 0, 0]
 
 
+def test_allreduce_oneshot_wait_runs_out(dev):
+    """A rank that never arrives: emulated tp = 3 on one GPU with rank 2's flags never raised and
+    a 1 ms wait limit.  The kernel gives up, records status 1 / role 20 and returns (the launch
+    succeeds and the context stays usable); the status is then cleared."""
+    import ctypes as C
+    from cuda_tempiler_b200 import _lib, ops
+    lib = _lib.load()
+    tp, cap, n, ctas, epoch = 3, 1024, 1024, 4, 1
+    recv = [torch.zeros(2 * tp * cap, dtype=torch.float16, device="cuda") for _ in range(tp)]
+    flags = [torch.zeros(tp * 32, dtype=torch.int32, device="cuda") for _ in range(tp)]
+    rp = (C.c_void_p * tp)(*[t.data_ptr() for t in recv])
+    fp = (C.c_void_p * tp)(*[t.data_ptr() for t in flags])
+    flags[0][1 * 32: 1 * 32 + ctas] = epoch  # rank 1 has delivered, rank 2 never will
+    y = torch.ones(n, dtype=torch.float16, device="cuda")
+    assert ops.device_status(reset=True) == [0, 0, 0, 0]
+    rc = lib.tempo_sm100_allreduce_oneshot_timed(y.data_ptr(), y.data_ptr(), n, cap, rp, fp, tp,
+                                                 0, epoch, ctas, 1_000_000,
+                                                 torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    st = ops.device_status(reset=True)
+    assert st[0] == 1 and st[1] == 20 and 0 <= st[2] < ctas and st[3] == 2, st
+    assert ops.device_status() == [0, 0, 0, 0]
+    # the context is still usable: a normal GEMM afterwards passes the gate
+    a, b = O.inputs_config1(64, 256, 256)
+    c = ops.gemm_fp16(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda())
+    assert O.rel_l2(c.cpu().numpy(), O.gemm_fp16_ref(a, b)) <= O.GATE_REL_L2
+    # out-of-range limits are refused without a launch
+    assert lib.tempo_sm100_allreduce_oneshot_timed(y.data_ptr(), y.data_ptr(), n, cap, rp, fp,
+                                                   tp, 0, epoch, ctas, 0, None) == 1
+
+
 def ops_status():
     from cuda_tempiler_b200 import ops
     return ops.device_status()
