@@ -1,8 +1,9 @@
 """Build the in-tree sm_100a shared library ``libtempo_sm100.so`` with nvcc.
 
-The library compiles the SHIPPED artifacts (kernels/shipped/<op>/sm_100a: kernel.cuh,
-launch.cuh, dispatch.inc) behind the C-ABI shim csrc/tempo_sm100.cu, as the reference's
-launch.cu compiles its shipped dispatch.inc.
+The library compiles the SHIPPED artifacts: csrc/tempo_sm100.cu (the C-ABI shim) includes the
+launch.cu of kernels/shipped/gemm_fp16/sm_100a and of kernels/shipped/gemm_w8a16/sm_100a, each
+of which brings its POD ABI (launch.cuh), the frozen kernels (kernel.cuh) and its generated
+dispatch body (dispatch.inc) -- the reference's launch.cu + dispatch.inc scheme.
 
 The library is the product: the CUDA kernels plus the extern "C" entry points declared in
 ``include/tempo_sm100.h``.  It is built in-tree so that it travels with the repository to the
@@ -20,7 +21,6 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 SHIPPED = PKG / "kernels" / "shipped"
-FP16_SHIP = SHIPPED / "gemm_fp16" / "sm_100a"
 LIB = PKG / "libtempo_sm100.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -33,7 +33,8 @@ def nvcc() -> str:
 
 
 def sources() -> list:
-    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(SHIPPED.glob("*/sm_100a/*.cuh"))
+    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh"))
+            + sorted(SHIPPED.glob("*/sm_100a/*.cuh")) + sorted(SHIPPED.glob("*/sm_100a/*.cu"))
             + sorted(SHIPPED.glob("*/sm_100a/*.inc")) + [INCLUDE / "tempo_sm100.h"])
 
 
@@ -50,7 +51,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     cmd = [
         nvcc(), *ARCH_FLAGS, "-O3", "-std=c++17", "-lineinfo", "-Xptxas", "-v",
-        "-Xcompiler", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{CSRC}", f"-I{SHIPPED}", f"-I{FP16_SHIP}",
+        "-Xcompiler", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{CSRC}", f"-I{SHIPPED}",
         "-o", str(LIB) + ".tmp", *[str(p) for p in sorted(CSRC.glob("*.cu"))],
     ]
     res = subprocess.run(cmd, capture_output=True, text=True)

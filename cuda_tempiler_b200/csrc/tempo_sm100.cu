@@ -13,140 +13,39 @@
 #include <mutex>
 
 #include "tempo_sm100.h"
-#include "launch.cuh"
+// The shipped artifacts, one translation unit: each op's launch.cu brings its POD ABI
+// (launch.cuh), the frozen device code (kernel.cuh) and host layer -- both include-guarded, so
+// the second op reuses the first's -- and tempo::gen::launch / plan around its generated
+// dispatch.inc.  Every GEMM entry point below goes through tempo::gen.
+#include "gemm_fp16/sm_100a/launch.cu"
+#include "gemm_w8a16/sm_100a/launch.cu"
 #include "elementwise.cuh"
 #include "collective.cuh"
 
 namespace tempo_sm100 {
 namespace {
 
-struct LadderRow {
-  int m_max;  // inclusive upper bound on M (0x7fffffff = everything else)
-  int bn, swap, group_m;
-  int cta_group;  // 1, or 2 for the 2-CTA 256 x BN prefill tiles (fp16)
-};
+constexpr size_t kPlanAnyWorkspace = (size_t)1 << 40;
 
-#include "gemm_fp16/sm_100a/dispatch.inc"
-#include "gemm_w8a16/sm_100a/dispatch.inc"
-
-const LadderRow* ladder_row(int wkind, int M) {
-  const LadderRow* rows = wkind == 0 ? kLadderFp16 : kLadderW8;
-  const int n = wkind == 0 ? (int)(sizeof(kLadderFp16) / sizeof(LadderRow))
-                           : (int)(sizeof(kLadderW8) / sizeof(LadderRow));
-  for (int i = 0; i < n; ++i)
-    if (M <= rows[i].m_max) return &rows[i];
-  return nullptr;
+tempo::gen::GemmParams fp16_params(const void* A, const void* B, void* C, int M, int N, int K,
+                                   int lda, int ldb, int ldc, void* ws, size_t ws_bytes) {
+  tempo::gen::GemmParams p{static_cast<const __half*>(A), static_cast<const __half*>(B),
+                           static_cast<__half*>(C), M, N, K, lda, ldb, ldc};
+  p.ws = ws;
+  p.ws_bytes = ws_bytes;
+  return p;
 }
 
-// Cycle model of one launch, used to pick the k-split (mirrored by the shipped select.py):
-//   SM side:  ceil(units / SMs) waves x (k-blocks per unit x per-k-block + split fix-up).
-//             Per k-block = max(MMA, operand feed): one 128xBNx16 UMMA costs max(BN/2 tensor
-//             cycles, (128+BN)*32 B / 128 B-per-cycle shared-memory reads); the feed is
-//             (128+BN)*128 B per k-block at ~100 B/cycle/SM from L2.  The split fix-up writes
-//             and re-reads a 128xBN fp32 slice (charged 3x for the counter/barrier).
-//   HBM side: compulsory bytes (2MK + w_b NK + 2MN) at ~3400 B/cycle for the whole GPU.
-//   launch:   the larger of the two.
-// Cycle model of one launch (the busiest SM): waves of units, each k-block costing the larger
-// of its UMMAs and its operand feed -- weight bytes stream from HBM at about 32 B/cycle per SM
-// (measured TMA streaming rate), activation bytes from L2 at about 100 -- plus the k-split
-// fixup: ~1500 cycles through distributed shared memory (splits <= kMaxClusterSplit), the
-// fp32 partial round trip through global memory beyond; never below the HBM time.
-double launch_cycles(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, int s,
-                     double hbm_bytes) {
-  const long long units = (long long)tiles * s;
-  const long long waves = (units + sms - 1) / sms;
-  const double mma = 4.0 * std::max(bn / 2.0, (128.0 + bn) / 4.0);
-  const double w_rows = swap ? 128.0 : bn, a_rows = swap ? bn : 128.0;
-  const double feed = w_rows * 64.0 * wbytes / 32.0 + a_rows * 128.0 / 100.0;
-  const double kb = (double)((num_kb + s - 1) / s);
-  const double fixup = s == 1 ? 0.0
-                     : s <= kMaxClusterSplit ? 1500.0
-                                             : 3.0 * 128.0 * bn * 4.0 / 100.0 + 1500.0;
-  const double sm_side = (double)waves * (kb * std::max(mma, feed) + fixup);
-  return std::max(sm_side, hbm_bytes / 3400.0);
-}
-
-int choose_splits(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, size_t ws_bytes,
-                  double hbm_bytes) {
-  if (sms <= 0) return 1;
-  int best = 1;
-  double best_c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, 1, hbm_bytes);
-  // the dispatcher keeps to cluster k-splits (the global-workspace path stays reachable as
-  // an explicit hyperform)
-  const int smax = std::min(kMaxClusterSplit, num_kb / 2);
-  for (int s = 2; s <= smax; ++s) {
-    if (ws_needed(tiles, s, bn) > ws_bytes) break;
-    // a cluster k-split launch is one CTA per unit, not persistent: one wave only
-    if (s <= kMaxClusterSplit && (long long)tiles * s > sms) continue;
-    const double c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, s, hbm_bytes);
-    if (c < best_c * 0.97) {
-      best = s;
-      best_c = c;
-    }
-  }
-  return best;
-}
-
-bool select_hyper(int wkind, int M, int N, int K, size_t ws_bytes, Hyper& h, int sms) {
-  const LadderRow* r = ladder_row(wkind, M);
-  if (!r) return false;
-  h.bn = r->bn;
-  h.swap = r->swap;
-  h.group_m = r->group_m;
-  h.max_ctas = 0;
-  h.cta_group = (wkind == 0 && r->cta_group == 2 && !r->swap) ? 2 : 1;
-  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  // a 128-wide 1-CTA row whose tiles overflow one wave takes the 256-wide tile (half the
-  // activation re-reads, one wave) when that instantiation exists
-  if (h.cta_group == 1 && !h.swap && h.bn == 128 && sms > 0 &&
-      (long long)((rows_p + 127) / 128) * ((rows_q + 127) / 128) > sms &&
-      find_inst(wkind, 256, 0) != nullptr)
-    h.bn = 256;
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
-  const int num_kb = (K + 63) / 64;
-  if (h.bn == 0) {  // streaming GEMV row of the ladder
-    h.splits = 1;
-    return M <= kGemvMaxM;
-  }
-  if (h.cta_group == 2) {  // pair tiles: width and split tail by the wave model
-    h.bn = choose_pair_bn(M, N, K, sms, h.bn, ws_bytes);
-    h.splits = 2;
-    return h.bn != 0;
-  }
-  const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
-  h.splits = choose_splits(tiles, num_kb, sms, h.bn, h.swap, wkind == 0 ? 2 : 1, ws_bytes, hbm);
-  return find_inst(wkind, h.bn, h.swap) != nullptr;
-}
-
-// Workspace bytes a hyperform needs (0: none) and, in *zero_bytes, how many leading bytes of it
-// are arrival counters that must be zero before a launch.
-size_t hyper_ws(int M, int N, int K, const Hyper& h, int sms, size_t ws_cap, size_t* zero_bytes) {
-  if (h.cta_group == 2) {
-    const PairPlan pl = pair_plan(M, N, K, h.bn, sms, h.max_ctas, h.splits > 1, ws_cap);
-    if (zero_bytes)
-      *zero_bytes = pl.ws_bytes ? counters_used_bytes(2 * (pl.tiles - pl.sk_tile0)) : 0;
-    return pl.ws_bytes;
-  }
-  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
-  const int bn = std::max(h.bn, 1);
-  const int tiles = ((rows_p + 127) / 128) * ((rows_q + bn - 1) / bn);
-  const size_t need = h.bn == 0 ? 0 : ws_needed(tiles, h.splits, h.bn);
-  if (zero_bytes) *zero_bytes = need ? counters_used_bytes(tiles) : 0;
-  return need;
-}
-
-cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  if (h.bn == 0) return run_gemv(pr, st, h.group_m);
-  if (h.cta_group == 2) return run_pair(pr, h, st);
-  const InstEntry* e = find_inst(pr.wkind, h.bn, h.swap);
-  if (!e) return cudaErrorInvalidConfiguration;
-  return e->fn(pr, h, st);
-}
-
-int current_sms() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  return dev_info(dev).sms;
+tempo::gen::W8A16Params w8_params(const void* A, const void* W, const void* scale,
+                                  const void* zero, void* C, int M, int N, int K, int lda,
+                                  int ldw, int ldc, int kind, int group, void* ws,
+                                  size_t ws_bytes) {
+  tempo::gen::W8A16Params p{static_cast<const __half*>(A), static_cast<const uint8_t*>(W),
+                            static_cast<const __half*>(scale), static_cast<const uint8_t*>(zero),
+                            static_cast<__half*>(C), M, N, K, lda, ldw, ldc, kind, group};
+  p.ws = ws;
+  p.ws_bytes = ws_bytes;
+  return p;
 }
 
 }  // namespace
@@ -158,66 +57,42 @@ extern "C" {
 
 int tempo_sm100_gemm_fp16_applicable(const void* A, const void* B, const void* C, int M, int N,
                                      int K, int lda, int ldb, int ldc) {
-  return fp16_applicable(A, B, C, M, N, K, lda, ldb, ldc) ? 1 : 0;
+  return tempo::gen::applicable(fp16_params(A, B, const_cast<void*>(C), M, N, K, lda, ldb, ldc,
+                                            nullptr, 0)) ? 1 : 0;
 }
 
 int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, int K, int lda,
                           int ldb, int ldc, void* ws, size_t ws_bytes, void* stream) {
-  if (!fp16_applicable(A, B, C, M, N, K, lda, ldb, ldc)) return cudaErrorInvalidConfiguration;
-  if (ws && !aligned16(ws)) return cudaErrorInvalidValue;  // counters, fp32 partials
-  Hyper h{};
-  if (!select_hyper(0, M, N, K, ws ? ws_bytes : 0, h, current_sms()))
-    return cudaErrorInvalidConfiguration;
-  Problem pr{0, A, B, nullptr, nullptr, C, M, N, K, lda, ldb, ldc, 0, ws, ws_bytes};
-  return run(pr, h, static_cast<cudaStream_t>(stream));
+  return tempo::gen::launch(fp16_params(A, B, C, M, N, K, lda, ldb, ldc, ws, ws_bytes),
+                            static_cast<cudaStream_t>(stream));
 }
 
 int tempo_sm100_gemm_w8a16_applicable(const void* A, const void* W, const void* scale,
                                       const void* zero, const void* C, int M, int N, int K,
                                       int lda, int ldw, int ldc, int quant_kind, int group_size) {
-  return w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, quant_kind, group_size) ? 1
-                                                                                              : 0;
+  return tempo::gen::applicable(w8_params(A, W, scale, zero, const_cast<void*>(C), M, N, K, lda,
+                                          ldw, ldc, quant_kind, group_size, nullptr, 0)) ? 1 : 0;
 }
 
 int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, const void* zero,
                            void* C, int M, int N, int K, int lda, int ldw, int ldc, int quant_kind,
                            int group_size, void* ws, size_t ws_bytes, void* stream) {
-  if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, quant_kind, group_size))
-    return cudaErrorInvalidConfiguration;
-  // the expanded weights are written with 16-byte stores from the start of ws
-  if (ws && !aligned16(ws)) return cudaErrorInvalidValue;
-  const int sms = current_sms();
-  if (M >= kExpandMinM && ws) {
-    // expanded weights at the front of the workspace, the fp16 launch's workspace behind them
-    const size_t wexp = expand_ws_bytes(N, K);
-    Hyper hf{};
-    if (ws_bytes >= wexp && select_hyper(0, M, N, K, ws_bytes - wexp, hf, sms)) {
-      cudaStream_t st = static_cast<cudaStream_t>(stream);
-      Problem pw{quant_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, wexp};
-      __half* wf = static_cast<__half*>(ws);
-      cudaError_t e = launch_expand(pw, wf, st);
-      if (e != cudaSuccess) return e;
-      Problem pr{0, A, wf, nullptr, nullptr, C, M, N, K, lda, K, ldc, 0,
-                 static_cast<char*>(ws) + wexp, ws_bytes - wexp};
-      return run(pr, hf, st);
-    }
-  }
-  Hyper h{};
-  if (!select_hyper(quant_kind, M, N, K, ws ? ws_bytes : 0, h, current_sms()))
-    return cudaErrorInvalidConfiguration;
-  Problem pr{quant_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
-  return run(pr, h, static_cast<cudaStream_t>(stream));
+  return tempo::gen::launch(w8_params(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, quant_kind,
+                                      group_size, ws, ws_bytes),
+                            static_cast<cudaStream_t>(stream));
 }
 
 size_t tempo_sm100_workspace_bytes(int M, int N, int K, int weight_kind) {
-  Hyper h{};
-  const int sms = current_sms();
-  if (weight_kind != 0 && M >= kExpandMinM && (K % 16) == 0) {  // expanded weights + fp16 launch
-    if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, sms)) return 0;
-    return expand_ws_bytes(N, K) + hyper_ws(M, N, K, h, sms, (size_t)1 << 40, nullptr);
-  }
-  if (!select_hyper(weight_kind, M, N, K, (size_t)1 << 40, h, sms)) return 0;
-  return hyper_ws(M, N, K, h, sms, (size_t)1 << 40, nullptr);
+  tempo::gen::Choice c{};
+  cudaError_t e;
+  if (weight_kind == 0)
+    e = tempo::gen::plan(fp16_params(nullptr, nullptr, nullptr, M, N, K, K, K, N, nullptr,
+                                     kPlanAnyWorkspace), &c);
+  else
+    e = tempo::gen::plan(w8_params(nullptr, nullptr, nullptr, nullptr, nullptr, M, N, K, K,
+                                   (K + 15) / 16 * 16, N, weight_kind, 64, nullptr,
+                                   kPlanAnyWorkspace), &c);
+  return e == cudaSuccess ? c.ws_bytes : 0;
 }
 
 int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, const void* scale,
@@ -245,32 +120,38 @@ int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W,
     return tempo_sm100_gemm_hyperform(weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc,
                                       group_size, bn, swap, splits, group_m, max_ctas, ws, ws_bytes,
                                       stream);
-  if (weight_kind != 0 || swap) return cudaErrorInvalidConfiguration;
-  if (!fp16_applicable(A, W, C, M, N, K, lda, ldw, ldc)) return cudaErrorInvalidConfiguration;
-  Hyper h{bn, 0, splits > 1 ? 2 : 1, group_m < 1 ? 1 : group_m, max_ctas};
+  if (swap) return cudaErrorInvalidConfiguration;
+  if (weight_kind == 0) {
+    if (!fp16_applicable(A, W, C, M, N, K, lda, ldw, ldc)) return cudaErrorInvalidConfiguration;
+  } else if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, ldc, weight_kind,
+                            group_size)) {
+    return cudaErrorInvalidConfiguration;
+  }
+  // W8A16 pair tiles take whole tiles only (no split tail)
+  Hyper h{bn, 0, (splits > 1 && weight_kind == 0) ? 2 : 1, group_m < 1 ? 1 : group_m, max_ctas};
   h.cta_group = 2;
-  Problem pr{0, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
+  Problem pr{weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
   return run(pr, h, static_cast<cudaStream_t>(stream));
 }
 
 int tempo_sm100_pair_resources(int bn, int* out6) { return pair_resources(bn, out6); }
 
 int tempo_sm100_select(int weight_kind, int M, int N, int K, size_t ws_bytes, int* out5) {
-  Hyper h{};
-  const int sms = current_sms();
-  if (weight_kind != 0 && M >= kExpandMinM && ws_bytes >= expand_ws_bytes(N, K) &&
-      select_hyper(0, M, N, K, ws_bytes - expand_ws_bytes(N, K), h, sms)) {
-    weight_kind = 0;  // expanded weights: the fp16 launch's configuration
-  } else if (!select_hyper(weight_kind, M, N, K, ws_bytes, h, sms)) {
-    return cudaErrorInvalidConfiguration;
-  }
-  const InstEntry* e = find_inst(weight_kind, h.bn, h.swap);
+  tempo::gen::Choice c{};
+  const cudaError_t e =
+      weight_kind == 0
+          ? tempo::gen::plan(fp16_params(nullptr, nullptr, nullptr, M, N, K, K, K, N, nullptr,
+                                         ws_bytes), &c)
+          : tempo::gen::plan(w8_params(nullptr, nullptr, nullptr, nullptr, nullptr, M, N, K, K,
+                                       (K + 15) / 16 * 16, N, weight_kind, 64, nullptr,
+                                       ws_bytes), &c);
+  if (e != cudaSuccess) return e;
   if (out5) {
-    out5[0] = h.bn;
-    out5[1] = h.swap;
-    out5[2] = h.splits;
-    out5[3] = h.group_m;
-    out5[4] = e ? e->stages : 0;
+    out5[0] = c.bn;
+    out5[1] = c.swap;
+    out5[2] = c.splits;
+    out5[3] = c.group_m;
+    out5[4] = c.stages;
   }
   return 0;
 }
@@ -336,7 +217,7 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
                                   const void* zero, void* C, int M, int N, int K, int lda, int ldw,
                                   int ldc, int quant_kind, int group_size, void* ws,
                                   size_t ws_bytes, void* stream) {
-  if (M < kExpandMinM || N % 128 || !ws || ws_bytes < expand_ws_bytes(N, K))
+  if (M < kExpandMinM || N % 128 || !ws || ws_bytes < kExpandOffset + expand_ws_bytes(N, K))
     return cudaErrorInvalidConfiguration;
   if (!aligned16(ws)) return cudaErrorInvalidValue;
   if (!w8_applicable(A, W, scale, zero, C, M, N, K, lda, ldw, N, quant_kind, group_size) ||
@@ -344,7 +225,8 @@ int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scal
     return cudaErrorInvalidConfiguration;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Problem pw{quant_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
-  __half* wf = static_cast<__half*>(ws);
+  // the copy after the counter prefix, which stays as the workspace's other users left it
+  __half* wf = reinterpret_cast<__half*>(static_cast<char*>(ws) + kExpandOffset);
   cudaError_t e = launch_expand(pw, wf, st);
   if (e != cudaSuccess) return e;
   Problem pr{0, A, wf, nullptr, nullptr, C, M, N, K, lda, K, ldc, 0, nullptr, 0};
@@ -452,7 +334,8 @@ void* g_noalloc_ptr[tempo_sm100::kMaxDevices];
 extern "C" int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void* C, int M, int N,
                                              int K, int lda, int ldb, int ldc, void* stream) {
   using namespace tempo_sm100;
-  if (!fp16_applicable(A, B, C, M, N, K, lda, ldb, ldc)) return cudaErrorInvalidConfiguration;
+  if (!tempo::gen::applicable(fp16_params(A, B, C, M, N, K, lda, ldb, ldc, nullptr, 0)))
+    return cudaErrorInvalidConfiguration;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -468,12 +351,14 @@ extern "C" int tempo_sm100_gemm_fp16_noalloc(const void* A, const void* B, void*
   void* scratch = g_noalloc_ptr[dev];
 
   // Same choice as tempo_sm100_gemm_fp16 given a workspace of tempo_sm100_workspace_bytes.
-  Hyper h{};
-  const int sms = current_sms();
-  if (!select_hyper(0, M, N, K, (size_t)1 << 40, h, sms)) return cudaErrorInvalidConfiguration;
-  size_t zero_bytes = 0;
-  const size_t need = hyper_ws(M, N, K, h, sms, (size_t)1 << 40, &zero_bytes);
+  tempo::gen::Choice c{};
+  e = tempo::gen::plan(fp16_params(A, B, C, M, N, K, lda, ldb, ldc, nullptr, kPlanAnyWorkspace),
+                       &c);
+  if (e != cudaSuccess) return e;
+  const size_t need = c.ws_bytes, zero_bytes = c.zero_bytes;
   if (need > (size_t)TEMPO_SM100_NOALLOC_SCRATCH_BYTES) return cudaErrorInvalidValue;
+  Hyper h{c.bn, c.swap, c.splits, c.group_m, 0};
+  h.cta_group = c.cta_group;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (need > 0) {
     // The counters must start at zero; the array keeps whatever the previous call left.

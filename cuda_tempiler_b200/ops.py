@@ -16,6 +16,8 @@ from . import _lib
 from ._lib import NotCovered, W8_INT8_PER_CHANNEL, W8_UINT8_GROUP  # noqa: F401
 
 _ws_cache: dict = {}
+# the W8A16 prefill's fp16 weight copy starts after the workspace's 64 KiB counter prefix
+EXPAND_OFFSET = 65536
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -214,7 +216,7 @@ def gemm_w8a16_swiglu(A: torch.Tensor, W: torch.Tensor, scale: torch.Tensor,
     kind = W8_INT8_PER_CHANNEL if W.dtype == torch.int8 else W8_UINT8_GROUP
     if out is None:
         out = torch.empty((M, N // 2), dtype=torch.float16, device=A.device)
-    ws = workspace(A.device, N * K * 2)
+    ws = workspace(A.device, EXPAND_OFFSET + N * K * 2)
     rc = lib.tempo_sm100_gemm_w8a16_swiglu(
         _ptr(A), _ptr(W), _ptr(scale.contiguous()),
         _ptr(zero.contiguous() if zero is not None else None), _ptr(out), M, N, K, A.stride(0),

@@ -256,7 +256,9 @@ def cmd_ship(a):
             measured = m0.get("rows", [])
         else:
             lad, measured = list(ship.DEFAULT_LADDER), []
-        m = ship.write_ship(op, lad, root, build_facts=facts, measured=measured)
+        m0 = json.load(open(prev)) if os.path.exists(prev) else {}
+        m = ship.write_ship(op, lad, root, build_facts=facts, measured=measured,
+                            gate=m0.get("gate"), card=m0.get("card"))
         print(f"shipped {op}: ladder {m['ladder']}")
     if facts:
         d = os.path.join(os.path.dirname(ship.__file__), "data", "build_facts.json")

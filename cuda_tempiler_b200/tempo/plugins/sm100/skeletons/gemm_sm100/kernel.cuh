@@ -1372,39 +1372,65 @@ __device__ __forceinline__ void tile_pos(const GemmArgs& a, int tile, int& tp, i
   tq = r / gm;
 }
 
-template <int BN_>
+template <int BN_, int WQ_ = 0>
 struct PairCfg {
-  static constexpr int BM = 128, BN = BN_, BK = 64;
+  static constexpr int BM = 128, BN = BN_, BK = 64, WQ = WQ_;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's fp16 B half of a k-block
   static constexpr int B_OFF = A_BYTES;
-  static constexpr int STAGE_BYTES = A_BYTES + round_up(B_BYTES, 1024);
+  // W8A16: the raw 8-bit B half [BN/2][64] (unswizzled 64-byte rows) that the dequant warps
+  // turn into the fp16 B half, then (group-wise) the stage's scale row (fp16) and zero row
+  // (uint8) for those BN/2 weight rows
+  static constexpr int RAW_OFF = B_OFF + round_up(B_BYTES, 1024);
+  static constexpr int RAW_BYTES = WQ ? (BN / 2) * BK : 0;
+  static constexpr int S_OFF = RAW_OFF + RAW_BYTES;
+  static constexpr int Z_OFF = S_OFF + (BN / 2) * 2;
+  static constexpr int SZ_BYTES = WQ == 2 ? (BN / 2) * 3 : 0;
+  static constexpr int STAGE_BYTES =
+      WQ ? RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024) : A_BYTES + round_up(B_BYTES, 1024);
   static constexpr int EPI_BYTES = 4 * 2 * 2048;
   static constexpr int BAR_BYTES = 512;
   static constexpr int STAGES = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 8);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-  static constexpr int THREADS = 192;
+  static constexpr int DEQ_WARPS = WQ ? 8 : 0;  // warps 6 .. 13 of a W8A16 CTA
+  static constexpr int THREADS = 192 + 32 * DEQ_WARPS;
+  // raw 16-byte chunks of a stage's B half, and how many each dequant thread converts
+  static constexpr int DEQ_CHUNKS = WQ ? RAW_BYTES / 16 : 0;
+  static constexpr int DEQ_PER_THREAD = WQ ? DEQ_CHUNKS / (32 * DEQ_WARPS) : 1;
+  // barriers: full[S], empty[S], tfull[2], tempty[2], done, then (W8A16) raw[S], deq[S]
+  static constexpr int NBARS = 2 * STAGES + 5 + (WQ ? 2 * STAGES : 0);
   // accumulator buffer b starts at TMEM column b * ACC_STRIDE (a power of two)
   static constexpr int ACC_STRIDE = BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = tmem_cols_for(2 * ACC_STRIDE);
   static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256,
                 "pair tiles are 256 x BN, BN in 128..256 step 32 (32-column epilogue chunks)");
-  static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
+  static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
+  static_assert(!WQ || DEQ_CHUNKS % (32 * DEQ_WARPS) == 0, "dequant chunks split evenly");
+  static_assert(SMEM <= kMaxDynSmem, "shared memory");
 };
 
-template <int BN, bool SWIGLU>
-__global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
+// WQ != 0 (W8A16): mapB covers the raw 8-bit weights [N][K]; each CTA's 8 dequant warps turn
+// its raw B half into the fp16 B half of the stage in shared memory (generic-proxy stores,
+// fence.proxy.async, then an arrive on the leader's deq barrier, whose count is both CTAs'
+// dequant warps), and the leader's MMA waits for A (full) and both dequantised halves (deq).
+// mapS / mapZ (group-wise) are the scale [K/g][N] fp16 and zero [K/g][N] uint8 rows; the
+// per-channel scale is applied in the epilogue.  No split tail and no SwiGLU with WQ.
+template <int BN, bool SWIGLU, int WQ = 0>
+__global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
     k_gemm_sm100_pair(const __grid_constant__ CUtensorMap mapA,
                       const __grid_constant__ CUtensorMap mapB,
-                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
-  using Cfg = PairCfg<BN>;
+                      const __grid_constant__ CUtensorMap mapC,
+                      const __grid_constant__ CUtensorMap mapS,
+                      const __grid_constant__ CUtensorMap mapZ, const GemmArgs args) {
+  using Cfg = PairCfg<BN, WQ>;
+  static_assert(!(SWIGLU && WQ), "the fused SwiGLU epilogue is fp16-only");
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* epi_smem = smem + STAGES * Cfg::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -1419,6 +1445,8 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
   auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
   auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
   const uint32_t done_bar = bar_base + 8u * (2 * STAGES + 4);
+  auto raw_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 5 + s); };
+  auto deq_bar = [&](int s) { return bar_base + 8u * (3 * STAGES + 5 + s); };
   auto a_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES; };
   auto b_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::B_OFF; };
 
@@ -1429,6 +1457,10 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);   // leader: its own arrive.expect_tx + both CTAs' bytes
       mbar_init(empty_bar(s), 1);  // multicast commit from the leader's MMA thread
+      if (WQ) {
+        mbar_init(raw_bar(s), 1);                   // this CTA's raw weight (+ scale/zero) bytes
+        mbar_init(deq_bar(s), 2 * Cfg::DEQ_WARPS);  // leader: both CTAs' dequant warps
+      }
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
@@ -1442,6 +1474,10 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapB);
     tma_prefetch_desc(&mapC);
+    if (WQ == kWUint8Group) {
+      tma_prefetch_desc(&mapS);
+      tma_prefetch_desc(&mapZ);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -1470,11 +1506,26 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         bool ok = true;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, 11)) { ok = false; break; }
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
           const uint32_t lead_full = mapa_shared(full_bar(stage), 0);
           const int kx = kb * Cfg::BK;
-          tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
-          tma_load_2d_pair(b_addr(stage), &mapB, lead_full, kx, tq * BN + (int)rank * (BN / 2), pol);
+          const int nrow = tq * BN + (int)rank * (BN / 2);
+          if (WQ == 0) {
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
+            tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
+            tma_load_2d_pair(b_addr(stage), &mapB, lead_full, kx, nrow, pol);
+          } else {
+            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::A_BYTES);
+            tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
+            // the raw weights (and their group's scale / zero rows) land in this CTA only
+            const uint32_t sb = a_addr(stage);
+            mbar_arrive_expect_tx(raw_bar(stage), Cfg::RAW_BYTES + Cfg::SZ_BYTES);
+            tma_load_2d(sb + Cfg::RAW_OFF, &mapB, raw_bar(stage), kx, nrow, pol);
+            if (WQ == kWUint8Group) {
+              const int g = kx / args.group_size;
+              tma_load_2d(sb + Cfg::S_OFF, &mapS, raw_bar(stage), nrow, g, pol);
+              tma_load_2d(sb + Cfg::Z_OFF, &mapZ, raw_bar(stage), nrow, g, pol);
+            }
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -1483,8 +1534,9 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         }
         if (!ok) break;
       }
-      // Drain: the leader's full barriers see every byte both CTAs requested.
-      if (leader) {
+      // Drain: the leader's full barriers see every byte both CTAs requested; each CTA's raw
+      // barriers (W8A16) every byte of its own weight loads.
+      {
         const int pending = issued < STAGES ? issued : STAGES;
         int s = stage;
         uint32_t ph = phase;
@@ -1493,7 +1545,8 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
             s = STAGES - 1;
             ph ^= 1u;
           }
-          mbar_drain(full_bar(s), ph, 100000000ull);
+          if (leader) mbar_drain(full_bar(s), ph, 100000000ull);
+          if (WQ) mbar_drain(raw_bar(s), ph, 100000000ull);
         }
       }
     }
@@ -1516,6 +1569,7 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         bool ok = true;
         for (int kb = kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 13)) { ok = false; break; }
+          if (WQ && !mbar_wait_cluster(deq_bar(stage), phase, abort_flag, 18)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k)
@@ -1533,6 +1587,71 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       }
       umma_commit_pair_mc(done_bar, 0x1);
       mbar_drain(done_bar, 0, 100000000ull);
+    }
+  } else if (WQ && warp >= 6) {
+    // ------------------------------------------------------------------ dequant (W8A16, both)
+    // Thread t of the 256 converts raw chunks c = t, t + 256, ...: 16 bytes = 16 weights of
+    // row c / 4, k-range 16 (c % 4); its fp16 results are the row's 16-byte granules 2 (c % 4)
+    // and 2 (c % 4) + 1, stored at granule ^ (row & 7) (the 128-byte swizzle TMA would have
+    // produced).  Consecutive lanes read consecutive 16 bytes, and a warp's stores cover every
+    // granule position of its 8 rows once per pass: no bank conflicts.
+    const int t = threadIdx.x - 192;
+    const uint32_t lead_deq = mapa_shared(deq_bar(0), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    PairSegIter segs(args, cluster, nclusters);
+    PairSeg sg;
+    bool ok = true;
+    while (ok && segs.next(args, sg)) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+        if (!mbar_wait(raw_bar(stage), phase, abort_flag, 17)) { ok = false; break; }
+        uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
+        const uint8_t* raw = sb + Cfg::RAW_OFF;
+        uint8_t* dst = sb + Cfg::B_OFF;
+        uint4 x[Cfg::DEQ_PER_THREAD];
+#pragma unroll
+        for (int i = 0; i < Cfg::DEQ_PER_THREAD; ++i)
+          x[i] = *reinterpret_cast<const uint4*>(raw + (t + 256 * i) * 16);
+#pragma unroll
+        for (int i = 0; i < Cfg::DEQ_PER_THREAD; ++i) {
+          const int c = t + 256 * i;
+          const int row = c >> 2, kq = c & 3;
+          __half2 h[8];
+          if (WQ == kWInt8PerChannel) {
+            // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
+            const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+            u8x4_to_h2x2_biased(x[i].x ^ 0x80808080u, h[0], h[1]);
+            u8x4_to_h2x2_biased(x[i].y ^ 0x80808080u, h[2], h[3]);
+            u8x4_to_h2x2_biased(x[i].z ^ 0x80808080u, h[4], h[5]);
+            u8x4_to_h2x2_biased(x[i].w ^ 0x80808080u, h[6], h[7]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) h[j] = __hsub2(h[j], bias);
+          } else {
+            // (1024 + q) - (1024 + z) = q - z exactly, then one rounding in the scale product;
+            // rows past N were zero-filled by TMA (s = 0), so their weights are 0
+            const __half2 zb =
+                __half2half2(__ushort_as_half((unsigned short)(0x6400u | sb[Cfg::Z_OFF + row])));
+            const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[row]);
+            u8x4_to_h2x2_biased(x[i].x, h[0], h[1]);
+            u8x4_to_h2x2_biased(x[i].y, h[2], h[3]);
+            u8x4_to_h2x2_biased(x[i].z, h[4], h[5]);
+            u8x4_to_h2x2_biased(x[i].w, h[6], h[7]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) h[j] = __hmul2(__hsub2(h[j], zb), s2);
+          }
+          const uint4* hv = reinterpret_cast<const uint4*>(h);
+          uint8_t* drow = dst + row * 128;
+          *reinterpret_cast<uint4*>(drow + (((2 * kq) ^ (row & 7)) * 16)) = hv[0];
+          *reinterpret_cast<uint4*>(drow + (((2 * kq + 1) ^ (row & 7)) * 16)) = hv[1];
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> the MMA's async-proxy reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_deq + 8u * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue (both)
@@ -1564,7 +1683,7 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
         if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
         continue;
       }
-      if (sg.contrib > 1) {
+      if (WQ == 0 && sg.contrib > 1) {
         // Tail k-slice: this CTA's 128 x BN fp32 partial goes to slot (slice, t), laid out
         // [32-column chunk][row][32] so each thread writes and reads its row's 128 contiguous
         // bytes per chunk as float4s.  The last of the tile's k-slices to arrive keeps its own
@@ -1715,6 +1834,13 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
       for (int c = 0; c < nchunk; ++c) {
         float f[32];
         acc_chunk<32, 1, BN>(t_acc, c, f);
+        if (WQ == kWInt8PerChannel) {
+          // per-output-channel scale of columns q0 + 32 c + j: lane j loads one, all share it
+          const int n = q0 + c * 32 + lane;
+          const float sv = n < args.rows_q ? __half2float(__ldg(args.scale + n)) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] *= __shfl_sync(0xffffffffu, sv, j);
+        }
         if (c == nchunk - 1) {
           tc_fence_before();
           __syncwarp();

@@ -1,8 +1,10 @@
-// launch.cuh -- host side of the sm_100a GEMM skeleton family: TMA descriptor construction,
-// the instantiation table (one entry per (BN, weight kind, swap) hyperform family member),
-// the persistent-grid launch and the applicability predicates.  Mirrors the reference's
-// shipped launch.cuh (kernels/shipped/gemm_fp16/sm_70/launch.cuh:20-67: POD params,
-// launch_one<...> with the >48 KB dynamic shared-memory opt-in, applicable()).
+// launch.cuh -- host layer of the sm_100a GEMM skeleton family: TMA descriptor construction,
+// the instantiation table (one entry per (BN, weight kind, swap) hyperform family member), the
+// persistent-grid and 2-CTA launches, the work planners and the ladder-row dispatcher engine.
+// Everything here has internal linkage: the ship stage freezes it into the first half of each
+// shipped launch.cu (the single translation unit that instantiates the kernels, as the
+// reference's kernels/shipped/gemm_fp16/sm_70/launch.cu is); the public POD ABI is the
+// separate shipped launch.cuh.
 #pragma once
 
 #include <cuda.h>
@@ -172,8 +174,12 @@ struct Problem {
   int M, N, K;
   long long lda, ldw, ldc;
   int group;
-  void* ws;
-  size_t ws_bytes;
+  void* ws;         // workspace: the arrival-counter prefix at its start
+  size_t ws_bytes;  // bytes of it for counters + fp32 partials
+  // where the fp32 partials start; nullptr: right after the counter prefix.  The W8A16
+  // prefill puts its expanded weights between the two, so that nothing but counters ever
+  // occupies the prefix of a workspace a caller reuses across problems.
+  void* ws_parts = nullptr;
 };
 
 struct Hyper {
@@ -244,7 +250,8 @@ cudaError_t launch_inst(const Problem& pr, const Hyper& h, cudaStream_t st) {
   if (a.splits > kMaxClusterSplit) {
     if (!pr.ws || pr.ws_bytes < ws_needed(tiles, a.splits, BN)) return cudaErrorInvalidValue;
     a.counters = static_cast<int*>(pr.ws);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
+    a.ws = reinterpret_cast<float*>(pr.ws_parts ? static_cast<char*>(pr.ws_parts)
+                                                : static_cast<char*>(pr.ws) + kCounterBytes);
   }
   a.scale = static_cast<const __half*>(pr.scale);
   a.zero = static_cast<const uint8_t*>(pr.zero);
@@ -415,6 +422,10 @@ constexpr int kExpandMinM = 512;
 
 size_t expand_ws_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 256; }
 
+// The expanded weights sit right after the counter prefix of the workspace (never at its
+// start: a workspace reused by a later split-K launch must still hold zeroed counters there).
+constexpr size_t kExpandOffset = kCounterBytes;
+
 cudaError_t launch_expand(const Problem& pr, __half* out, cudaStream_t st) {
   const long long n = (long long)pr.N * (pr.K / 16);
   const unsigned grid = (unsigned)((n + 255) / 256);
@@ -518,10 +529,10 @@ PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool spli
 
 // 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs; h.splits > 1
 // allows the split tail of pair_plan.
-template <int BN, bool SWIGLU = false>
+template <int BN, bool SWIGLU = false, int WQ = 0>
 cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  using Cfg = PairCfg<BN>;
-  auto kern = k_gemm_sm100_pair<BN, SWIGLU>;
+  using Cfg = PairCfg<BN, WQ>;
+  auto kern = k_gemm_sm100_pair<BN, SWIGLU, WQ>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -535,11 +546,14 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     });
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
   }
-  if (pr.wkind != 0 || h.swap) return cudaErrorInvalidConfiguration;
+  if (pr.wkind != WQ || h.swap) return cudaErrorInvalidConfiguration;
   if (SWIGLU && (pr.N % 128 || (BN != 128 && BN != 256))) return cudaErrorInvalidConfiguration;
-  // the fused SwiGLU epilogue has no split tail (its partial sums would be pre-activation)
+  if (WQ == kWUint8Group && (pr.group <= 0 || pr.group % Cfg::BK || pr.K % pr.group))
+    return cudaErrorInvalidConfiguration;
+  // the fused SwiGLU epilogue has no split tail (its partial sums would be pre-activation), nor
+  // has W8A16 (its per-channel scale is applied in the whole tile's epilogue)
   const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas,
-                                !SWIGLU && h.splits > 1,
+                                !SWIGLU && WQ == 0 && h.splits > 1,
                                 pr.ws ? pr.ws_bytes : 0);
   GemmArgs a{};
   a.rows_p = pr.M;
@@ -554,26 +568,44 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.C = static_cast<__half*>(pr.C);
   a.ldc = pr.ldc;
   a.weight_rows = pr.N;
+  a.scale = static_cast<const __half*>(pr.scale);
+  a.zero = static_cast<const uint8_t*>(pr.zero);
+  a.group_size = pr.group > 0 ? pr.group : 1;
+  a.groups_per_row = pr.group > 0 ? pr.K / pr.group : 1;
   a.sk_tile0 = pl.sk_tile0;
   a.sk_tiles = pl.sk_tiles;
   a.sk_splits = pl.sk_splits;
   if (pl.sk_splits > 0) {
     if (!pr.ws || pr.ws_bytes < pl.ws_bytes) return cudaErrorInvalidValue;
     a.counters = static_cast<int*>(pr.ws);
-    a.ws = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kCounterBytes);
+    a.ws = reinterpret_cast<float*>(pr.ws_parts ? static_cast<char*>(pr.ws_parts)
+                                                : static_cast<char*>(pr.ws) + kCounterBytes);
   }
-  CUtensorMap mA, mB, mC;
+  CUtensorMap mA, mB, mC, mS, mZ;
   std::memset(&mA, 0, sizeof(mA));
   std::memset(&mB, 0, sizeof(mB));
   std::memset(&mC, 0, sizeof(mC));
+  std::memset(&mS, 0, sizeof(mS));
+  std::memset(&mZ, 0, sizeof(mZ));
   const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok = make_map(&mA, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-  ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (WQ == 0) {
+    ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    // raw weights: rows of 64 bytes, unswizzled (the dequant warps apply the swizzle)
+    ok &= make_map(&mB, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (WQ == kWUint8Group) {
+      const int ng = pr.K / pr.group;
+      ok &= make_map(&mS, pr.scale, F16, 2, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+      ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+  }
   ok &= make_map(&mC, pr.C, F16, 2, SWIGLU ? pr.N / 2 : pr.N, pr.M, pr.ldc, 32, 32,
                  CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
   return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mB, mC,
-                   a);
+                   mS, mZ, a);
 }
 
 cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
@@ -583,6 +615,20 @@ cudaError_t run_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     case 192: return launch_pair<192>(pr, h, st);
     case 160: return launch_pair<160>(pr, h, st);
     case 128: return launch_pair<128>(pr, h, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
+// 2-CTA W8A16 tiles (8-bit weights dequantised in shared memory by 8 warps per CTA).
+constexpr int kPairW8Bn[] = {256, 128};
+constexpr double kPairW8Eff[] = {1.0, 0.55};
+
+cudaError_t run_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  const bool pc = pr.wkind == kWInt8PerChannel;
+  if (!pc && pr.wkind != kWUint8Group) return cudaErrorInvalidConfiguration;
+  switch (h.bn) {
+    case 256: return pc ? launch_pair<256, false, 1>(pr, h, st) : launch_pair<256, false, 2>(pr, h, st);
+    case 128: return pc ? launch_pair<128, false, 1>(pr, h, st) : launch_pair<128, false, 2>(pr, h, st);
     default: return cudaErrorInvalidConfiguration;
   }
 }
@@ -613,15 +659,19 @@ constexpr double kPairEff[] = {1.0, 0.92, 0.82, 0.67, 0.55};
 // The 2-CTA tile width for an M x N x K problem: the smallest modelled time, pair_plan's cost
 // (whole waves, or waves plus a split tail that fits ws_bytes) times bn / 256 / efficiency.
 // bn_max caps the choice (the ladder row's bn).
-int choose_pair_bn(int M, int N, int K, int sms, int bn_max, size_t ws_bytes) {
+int choose_pair_bn(int M, int N, int K, int sms, int bn_max, size_t ws_bytes, int wkind = 0) {
   if (sms <= 0) return bn_max;  // no device to size waves for
+  const int* widths = wkind ? kPairW8Bn : kPairBn;
+  const double* eff = wkind ? kPairW8Eff : kPairEff;
+  const int nw = wkind ? 2 : 5;
   int best = 0;
   double best_c = 0;
-  for (int i = 0; i < 5; ++i) {
-    const int bn = kPairBn[i];
+  for (int i = 0; i < nw; ++i) {
+    const int bn = widths[i];
     if (bn > bn_max) continue;
-    const PairPlan pl = pair_plan(M, N, K, bn, sms, 0, true, ws_bytes);
-    const double c = pl.cost * bn / 256.0 / kPairEff[i];
+    // W8A16 pair tiles run whole tiles only (no split tail)
+    const PairPlan pl = pair_plan(M, N, K, bn, sms, 0, wkind == 0, ws_bytes);
+    const double c = pl.cost * bn / 256.0 / eff[i];
     if (best == 0 || c < best_c) {
       best = bn;
       best_c = c;
@@ -690,6 +740,123 @@ bool w8_applicable(const void* A, const void* W, const void* scale, const void* 
     if ((N % 16) || !aligned16(scale) || !aligned16(zero)) return false;  // TMA row strides
   }
   return true;
+}
+
+// ------------------------------------------------------------------------------------------
+// The dispatcher engine: one M-ladder row (generated into dispatch.inc from measured tuner
+// rows) plus the problem -> the hyperform to launch.  The k-split comes from a cycle model
+// (mirrored by the shipped select.py).
+// ------------------------------------------------------------------------------------------
+struct LadderRow {
+  int m_max;  // inclusive upper bound on M (0x7fffffff = everything else)
+  int bn, swap, group_m;
+  int cta_group;  // 1, or 2 for the 2-CTA 256 x BN prefill tiles (fp16)
+};
+
+// Cycle model of one launch (the busiest SM): waves of units, each k-block costing the larger
+// of its UMMAs and its operand feed -- weight bytes stream from HBM at about 32 B/cycle per SM
+// (measured TMA streaming rate), activation bytes from L2 at about 100 -- plus the k-split
+// fixup: ~1500 cycles through distributed shared memory (splits <= kMaxClusterSplit), the
+// fp32 partial round trip through global memory beyond; never below the HBM time
+// (compulsory bytes at ~3400 B/cycle for the whole GPU).
+double launch_cycles(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, int s,
+                     double hbm_bytes) {
+  const long long units = (long long)tiles * s;
+  const long long waves = (units + sms - 1) / sms;
+  const double mma = 4.0 * std::max(bn / 2.0, (128.0 + bn) / 4.0);
+  const double w_rows = swap ? 128.0 : bn, a_rows = swap ? bn : 128.0;
+  const double feed = w_rows * 64.0 * wbytes / 32.0 + a_rows * 128.0 / 100.0;
+  const double kb = (double)((num_kb + s - 1) / s);
+  const double fixup = s == 1 ? 0.0
+                     : s <= kMaxClusterSplit ? 1500.0
+                                             : 3.0 * 128.0 * bn * 4.0 / 100.0 + 1500.0;
+  const double sm_side = (double)waves * (kb * std::max(mma, feed) + fixup);
+  return std::max(sm_side, hbm_bytes / 3400.0);
+}
+
+int choose_splits(int tiles, int num_kb, int sms, int bn, int swap, int wbytes, size_t ws_bytes,
+                  double hbm_bytes) {
+  if (sms <= 0) return 1;
+  int best = 1;
+  double best_c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, 1, hbm_bytes);
+  // the dispatcher keeps to cluster k-splits (the global-workspace path stays reachable as
+  // an explicit hyperform)
+  const int smax = std::min(kMaxClusterSplit, num_kb / 2);
+  for (int s = 2; s <= smax; ++s) {
+    if (ws_needed(tiles, s, bn) > ws_bytes) break;
+    // a cluster k-split launch is one CTA per unit, not persistent: one wave only
+    if (s <= kMaxClusterSplit && (long long)tiles * s > sms) continue;
+    const double c = launch_cycles(tiles, num_kb, sms, bn, swap, wbytes, s, hbm_bytes);
+    if (c < best_c * 0.97) {
+      best = s;
+      best_c = c;
+    }
+  }
+  return best;
+}
+
+// The hyperform for `row` of weight kind `wkind` (0 fp16, else a W8 kind); false when the row
+// names no instantiation that exists (the caller's fallback).
+bool select_hyper(int wkind, const LadderRow& r, int M, int N, int K, size_t ws_bytes, Hyper& h,
+                  int sms) {
+  h.bn = r.bn;
+  h.swap = r.swap;
+  h.group_m = r.group_m;
+  h.max_ctas = 0;
+  h.cta_group = (r.cta_group == 2 && !r.swap) ? 2 : 1;
+  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
+  // a 128-wide 1-CTA row whose tiles overflow one wave takes the 256-wide tile (half the
+  // activation re-reads, one wave) when that instantiation exists
+  if (h.cta_group == 1 && !h.swap && h.bn == 128 && sms > 0 &&
+      (long long)((rows_p + 127) / 128) * ((rows_q + 127) / 128) > sms &&
+      find_inst(wkind, 256, 0) != nullptr)
+    h.bn = 256;
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + std::max(h.bn, 1) - 1) / std::max(h.bn, 1));
+  const int num_kb = (K + 63) / 64;
+  if (h.bn == 0) {  // streaming GEMV row of the ladder
+    h.splits = 1;
+    return M <= kGemvMaxM;
+  }
+  if (h.cta_group == 2) {  // pair tiles: width and (fp16) split tail by the wave model
+    h.bn = choose_pair_bn(M, N, K, sms, h.bn, ws_bytes, wkind);
+    h.splits = wkind == 0 ? 2 : 1;
+    if (wkind == kWUint8Group && (N % 16)) return false;  // scale/zero rows by TMA
+    return h.bn != 0;
+  }
+  const double hbm = 2.0 * M * K + (wkind == 0 ? 2.0 : 1.0) * N * K + 2.0 * M * N;
+  h.splits = choose_splits(tiles, num_kb, sms, h.bn, h.swap, wkind == 0 ? 2 : 1, ws_bytes, hbm);
+  return find_inst(wkind, h.bn, h.swap) != nullptr;
+}
+
+// Workspace bytes a hyperform needs (0: none) and, in *zero_bytes, how many leading bytes of it
+// are arrival counters that must be zero before a launch.
+size_t hyper_ws(int M, int N, int K, const Hyper& h, int sms, size_t ws_cap, size_t* zero_bytes) {
+  if (h.cta_group == 2) {
+    const PairPlan pl = pair_plan(M, N, K, h.bn, sms, h.max_ctas, h.splits > 1, ws_cap);
+    if (zero_bytes)
+      *zero_bytes = pl.ws_bytes ? counters_used_bytes(2 * (pl.tiles - pl.sk_tile0)) : 0;
+    return pl.ws_bytes;
+  }
+  const int rows_p = h.swap ? N : M, rows_q = h.swap ? M : N;
+  const int bn = std::max(h.bn, 1);
+  const int tiles = ((rows_p + 127) / 128) * ((rows_q + bn - 1) / bn);
+  const size_t need = h.bn == 0 ? 0 : ws_needed(tiles, h.splits, h.bn);
+  if (zero_bytes) *zero_bytes = need ? counters_used_bytes(tiles) : 0;
+  return need;
+}
+
+cudaError_t run(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  if (h.bn == 0) return run_gemv(pr, st, h.group_m);
+  if (h.cta_group == 2) return pr.wkind ? run_pair_w8(pr, h, st) : run_pair(pr, h, st);
+  const InstEntry* e = find_inst(pr.wkind, h.bn, h.swap);
+  if (!e) return cudaErrorInvalidConfiguration;
+  return e->fn(pr, h, st);
+}
+
+int current_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return dev_info(dev).sms;
 }
 
 }  // namespace

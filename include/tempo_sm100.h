@@ -17,8 +17,9 @@
  *   8 (16 bytes); base pointers 16-byte aligned; K and N multiples of 8.
  *
  * Workspace: split-K launches need `ws` (device memory, zero-filled once by the caller before
- * its first use).  Its first 64 KiB hold arrival counters, which every launch leaves at zero;
- * the rest holds fp32 partials, which need no clearing.  Query the size with
+ * its first use).  Its first 64 KiB hold arrival counters, which every launch leaves at zero
+ * and nothing else ever writes; the rest holds fp32 partials (and, for the W8A16 prefill, the
+ * fp16 copy of the weights right after the counters), which need no clearing.  Query the size with
  * tempo_sm100_workspace_bytes.  ws == NULL or too small is legal: the dispatcher then picks
  * a configuration without split-K.  A non-NULL ws must be 16-byte aligned (else 1,
  * cudaErrorInvalidValue, and nothing is launched).  One workspace must not be shared by
@@ -40,7 +41,10 @@ extern "C" {
 #define TEMPO_W8_UINT8_GROUP 2       /* uint8 W [N][K], fp16 scale/uint8 zero [K/g][N] (GPTQ's
                                         scales and byte view of qzeros); W = (q - z) * s      */
 
-/* Replaces tempo::gen::applicable(const GemmParams&) (launch.cuh:59-67).  1 = covered. */
+/* Replaces tempo::gen::applicable(const GemmParams&) (launch.cuh:59-67).  1 = covered.
+ * The C-ABI is a thin layer over the shipped POD ABI (kernels/shipped/<op>/sm_100a/launch.cuh:
+ * tempo::gen::GemmParams / W8A16Params, applicable(), launch(), plan()), for callers that bind
+ * C symbols (ctypes, cgo, JNI) rather than compile the ship directory into their own tree. */
 int tempo_sm100_gemm_fp16_applicable(const void* A, const void* B, const void* C, int M, int N,
                                      int K, int lda, int ldb, int ldc);
 
@@ -59,10 +63,10 @@ int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, i
 int tempo_sm100_gemm_w8a16_applicable(const void* A, const void* W, const void* scale,
                                       const void* zero, const void* C, int M, int N, int K,
                                       int lda, int ldw, int ldc, int quant_kind, int group_size);
-/* From M = 512 on, given a workspace of at least N * K * 2 bytes (tempo_sm100_workspace_bytes
- * asks for it), the weights are first expanded to fp16 in the workspace by an HBM-bound pass
- * and the fp16 2-CTA kernel runs on the copy; below that, or with less workspace, the 8-bit
- * weights are dequantised inside the tensor-core kernel (or the streaming GEMV for M <= 16). */
+/* From M = 512 on, given a workspace of at least 65536 + N * K * 2 bytes
+ * (tempo_sm100_workspace_bytes asks for it), the weights are first expanded to fp16 in the
+ * workspace by an HBM-bound pass and the fp16 2-CTA kernel runs on the copy; below that, or
+ * with less workspace, the 8-bit weights are dequantised inside the tensor-core kernel (or the streaming GEMV for M <= 16). */
 int tempo_sm100_gemm_w8a16(const void* A, const void* W, const void* scale, const void* zero,
                            void* C, int M, int N, int K, int lda, int ldw, int ldc, int quant_kind,
                            int group_size, void* ws, size_t ws_bytes, void* stream);
@@ -129,7 +133,7 @@ int tempo_sm100_silu_mul(const void* gu, void* out, int M, int I, int ld_gu, int
  * 64 t + j), N = 2 I a multiple of 128; C [M][I] = silu(A Wg^T) * (A Wu^T), ldc >= I.  Covers
  * M > 256 (2-CTA tiles); 9 below, where the GEMM plus tempo_sm100_silu_mul (block 64) is the
  * caller's path.  The W8A16 form (same quantisation arguments as tempo_sm100_gemm_w8a16, scales
- * and zero points permuted like the rows) covers M >= 512 with ws >= N * K * 2 bytes. */
+ * and zero points permuted like the rows) covers M >= 512 with ws >= 65536 + N * K * 2 bytes. */
 int tempo_sm100_gemm_fp16_swiglu(const void* A, const void* W, void* C, int M, int N, int K,
                                  int lda, int ldw, int ldc, void* stream);
 int tempo_sm100_gemm_w8a16_swiglu(const void* A, const void* W, const void* scale,

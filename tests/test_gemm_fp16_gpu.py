@@ -193,3 +193,24 @@ def test_lm_head_and_narrow_n(dev, M, N, K):
     ref = O.gemm_fp16_ref(a, b)
     assert O.rel_l2(c, ref) <= TOL
     assert ops.device_status() == [0, 0, 0, 0]
+
+
+def test_workspace_shared_with_w8a16_prefill(dev):
+    """One cached workspace serves a W8A16 prefill (which writes an fp16 copy of its weights
+    into the workspace) and then an fp16 launch with a split tail (which needs zeroed arrival
+    counters at the workspace's start): the copy sits after the counter prefix, so the fp16
+    result is right.  Before the copy moved there, the second launch read weight bytes as
+    counters and returned garbage."""
+    from cuda_tempiler_b200 import ops
+    a8, q, s = O.inputs_w8_per_channel(1024, 5120, 4096, seed=9)
+    sel = ops.select(1, 1024, 5120, 4096, 1 << 40)
+    c8 = ops.gemm_w8a16(torch.from_numpy(a8).cuda(), torch.from_numpy(q).cuda(),
+                        torch.from_numpy(s).cuda())
+    M, N, K = 300, 1024, 15360  # a split-tail problem (the planner cuts its only wave)
+    assert ops._lib.load().tempo_sm100_workspace_bytes(M, N, K, 0) > 0
+    a, b, c = _run(ops.gemm_fp16, M, N, K, seed=4)
+    _gate(a, b, c)
+    torch.cuda.synchronize()
+    assert O.rel_l2(c8.cpu().numpy(), O.gemm_w_ref(a8, O.dequant_per_channel(q, s))) <= TOL
+    assert sel["bn"] > 0
+    assert ops.device_status() == [0, 0, 0, 0]

@@ -175,3 +175,21 @@ def test_expand_path_prefill(dev, M, N, K):
     r = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_w8a16(A, W, s, z, G, out=C))
     assert r <= TOL, r
     assert ops.device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("M,N,K", [(256, 1024, 1024), (300, 784, 2048), (77, 528, 512),
+                                   (600, 2064, 1536)])
+def test_pair_tiles_w8(dev, bn, M, N, K):
+    """2-CTA W8A16 tiles (256 x bn, tcgen05.mma.cta_group::2): each CTA's 8 dequant warps turn
+    its raw 8-bit B half into fp16 in shared memory; per-channel (scale in the epilogue) and
+    group-wise (scale and zero point applied in the dequant), ragged M and N."""
+    from cuda_tempiler_b200 import ops
+    r1 = _pc(M, N, K, lambda A, W, s, C: ops.gemm_hyperform(
+        A, W, bn=bn, swap=False, cta_group=2, scale=s, out=C))
+    r2 = 0.0
+    if N % 16 == 0:
+        r2 = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+            A, W, bn=bn, swap=False, cta_group=2, scale=s, zero=z, group_size=G, out=C))
+    assert r1 <= TOL and r2 <= TOL, (r1, r2)
+    assert ops.device_status() == [0, 0, 0, 0]

@@ -29,14 +29,16 @@ def test_manifest_signs_every_file(op):
     assert ship.verify_ship(ROOT, op) == []
     m = json.load(open(os.path.join(ROOT, op, "sm_100a", "manifest.json")))
     assert m["schema"] == "tempo/shipped/1" and m["contract"] == "tempo/arch/1"
-    assert set(m["md5"]) == {"kernel.cuh", "launch.cuh", "dispatch.inc", "select.py"}
+    assert set(m["md5"]) == {"kernel.cuh", "launch.cuh", "launch.cu", "dispatch.inc", "select.py"}
 
 
 @pytest.mark.parametrize("op", OPS)
 def test_dispatch_matches_select(op):
     sel = load_select(op)
     inc = open(os.path.join(ROOT, op, "sm_100a", "dispatch.inc")).read()
-    rows = re.findall(r"\{(0x7fffffff|\d+), (\d+), (\d+), (\d+), (\d+)\}", inc)
+    table = inc[inc.index("kLadder[] = {"):]
+    table = table[:table.index("};")]
+    rows = re.findall(r"\{(0x7fffffff|\d+), (\d+), (\d+), (\d+), (\d+)\}", table)
     got = [[int(a, 0), int(b), int(c), int(d), int(e)] for a, b, c, d, e in rows]
     assert got == [list(r) for r in sel.LADDER]
     assert sel.LADDER[-1][0] >= 0x7FFFFFFF, "the last ladder row must cover every M"
