@@ -326,6 +326,41 @@ __device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 
+// Non-blocking probe of a phase with cluster-scope acquire.  try_wait may suspend the thread
+// until a hardware time limit when the completing arrive comes from another CTA of the
+// cluster; a barrier completed by remote arrivals every k-block is polled with test_wait.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded polling wait (test_wait) with cluster-scope acquire.
+__device__ __noinline__ bool mbar_poll_cluster(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, int where) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 1024; ++i)
+      if (mbar_test_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      if (atomicCAS(&g_status[0], 0, 1) == 0) {
+        g_status[1] = where;
+        g_status[2] = blockIdx.x;
+      }
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 // Stores into the shared memory of a CTA of this cluster (shared::cluster address).
 __device__ __forceinline__ void st_dsmem_f32(uint32_t cluster_addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
@@ -1833,11 +1868,11 @@ struct PairCfg {
   static constexpr int BAR_BYTES = 512;
   static constexpr int STAGES = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 8);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-  static constexpr int DEQ_WARPS = WQ ? 8 : 0;  // warps 6 .. 13 of a W8A16 CTA
+  // W8A16: one dequant warp per stage (warps 6 .. 5 + STAGES), each owning its stage
+  static constexpr int DEQ_WARPS = WQ ? STAGES : 0;
   static constexpr int THREADS = 192 + 32 * DEQ_WARPS;
-  // raw 16-byte chunks of a stage's B half, and how many each dequant thread converts
+  // raw 16-byte chunks of a stage's B half (a multiple of 4 x 32: one warp, 4 in flight)
   static constexpr int DEQ_CHUNKS = WQ ? RAW_BYTES / 16 : 0;
-  static constexpr int DEQ_PER_THREAD = WQ ? DEQ_CHUNKS / (32 * DEQ_WARPS) : 1;
   // barriers: full[S], empty[S], tfull[2], tempty[2], done, then (W8A16) raw[S], deq[S]
   static constexpr int NBARS = 2 * STAGES + 5 + (WQ ? 2 * STAGES : 0);
   // accumulator buffer b starts at TMEM column b * ACC_STRIDE (a power of two)
@@ -1846,7 +1881,7 @@ struct PairCfg {
   static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256,
                 "pair tiles are 256 x BN, BN in 128..256 step 32 (32-column epilogue chunks)");
   static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
-  static_assert(!WQ || DEQ_CHUNKS % (32 * DEQ_WARPS) == 0, "dequant chunks split evenly");
+  static_assert(!WQ || DEQ_CHUNKS % 128 == 0, "dequant chunks: whole passes of 4 per lane");
   static_assert(SMEM <= kMaxDynSmem, "shared memory");
 };
 
@@ -1900,7 +1935,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
       mbar_init(empty_bar(s), 1);  // multicast commit from the leader's MMA thread
       if (WQ) {
         mbar_init(raw_bar(s), 1);                   // this CTA's raw weight (+ scale/zero) bytes
-        mbar_init(deq_bar(s), 2 * Cfg::DEQ_WARPS);  // leader: both CTAs' dequant warps
+        mbar_init(deq_bar(s), 2);  // leader: the owning dequant warp of each CTA
       }
     }
     for (int b = 0; b < 2; ++b) {
@@ -2010,7 +2045,11 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         bool ok = true;
         for (int kb = kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 13)) { ok = false; break; }
-          if (WQ && !mbar_wait_cluster(deq_bar(stage), phase, abort_flag, 18)) { ok = false; break; }
+          if (WQ && !mbar_test_wait_cluster(deq_bar(stage), phase) &&
+              !mbar_poll_cluster(deq_bar(stage), phase, abort_flag, 18)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k)
@@ -2031,67 +2070,73 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
     }
   } else if (WQ && warp >= 6) {
     // ------------------------------------------------------------------ dequant (W8A16, both)
-    // Thread t of the 256 converts raw chunks c = t, t + 256, ...: 16 bytes = 16 weights of
-    // row c / 4, k-range 16 (c % 4); its fp16 results are the row's 16-byte granules 2 (c % 4)
-    // and 2 (c % 4) + 1, stored at granule ^ (row & 7) (the 128-byte swizzle TMA would have
-    // produced).  Consecutive lanes read consecutive 16 bytes, and a warp's stores cover every
-    // granule position of its 8 rows once per pass: no bank conflicts.
-    const int t = threadIdx.x - 192;
+    // Dequant warp d owns the stages s with s % DEQ_WARPS == d and converts each of them alone,
+    // so up to DEQ_WARPS stages are converted at once: the release of a stage to the leader
+    // (fence.proxy.async, then an arrive with cluster-scope release) waits for the warp's stores
+    // and takes far longer than the conversion, and owning whole stages overlaps those waits.
+    // Lane l converts raw chunks c = l + 32 i: 16 bytes = 16 weights of row c / 4, k-range
+    // 16 (c % 4); its fp16 results are the row's 16-byte granules 2 (c % 4) and 2 (c % 4) + 1,
+    // stored at granule ^ (row & 7) (the 128-byte swizzle TMA would have produced).  Reads are
+    // consecutive 16-byte chunks; each pass of stores covers every granule position of its 8
+    // rows once: no bank conflicts.
+    const int dw = warp - 6;
     const uint32_t lead_deq = mapa_shared(deq_bar(0), 0);
-    int stage = 0;
-    uint32_t phase = 0;
+    int sit = 0;  // stage-iteration sequence number, the same sequence as the producer's
     PairSegIter segs(args, cluster, nclusters);
     PairSeg sg;
     bool ok = true;
     while (ok && segs.next(args, sg)) {
-      for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++sit) {
+        const int stage = sit % STAGES;
+        if (stage % Cfg::DEQ_WARPS != dw) continue;  // a stage always has the same owner
+        const uint32_t phase = (uint32_t)((sit / STAGES) & 1);
         if (!mbar_wait(raw_bar(stage), phase, abort_flag, 17)) { ok = false; break; }
         uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
         const uint8_t* raw = sb + Cfg::RAW_OFF;
         uint8_t* dst = sb + Cfg::B_OFF;
-        uint4 x[Cfg::DEQ_PER_THREAD];
+#pragma unroll 1
+        for (int i0 = 0; i0 < Cfg::DEQ_CHUNKS / 32; i0 += 4) {
+          uint4 x[4];
 #pragma unroll
-        for (int i = 0; i < Cfg::DEQ_PER_THREAD; ++i)
-          x[i] = *reinterpret_cast<const uint4*>(raw + (t + 256 * i) * 16);
+          for (int u = 0; u < 4; ++u)
+            x[u] = *reinterpret_cast<const uint4*>(raw + (lane + 32 * (i0 + u)) * 16);
 #pragma unroll
-        for (int i = 0; i < Cfg::DEQ_PER_THREAD; ++i) {
-          const int c = t + 256 * i;
-          const int row = c >> 2, kq = c & 3;
-          __half2 h[8];
-          if (WQ == kWInt8PerChannel) {
-            // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
-            const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
-            u8x4_to_h2x2_biased(x[i].x ^ 0x80808080u, h[0], h[1]);
-            u8x4_to_h2x2_biased(x[i].y ^ 0x80808080u, h[2], h[3]);
-            u8x4_to_h2x2_biased(x[i].z ^ 0x80808080u, h[4], h[5]);
-            u8x4_to_h2x2_biased(x[i].w ^ 0x80808080u, h[6], h[7]);
+          for (int u = 0; u < 4; ++u) {
+            const int c = lane + 32 * (i0 + u);
+            const int row = c >> 2, kq = c & 3;
+            __half2 h[8];
+            if (WQ == kWInt8PerChannel) {
+              // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
+              const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+              u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[0], h[1]);
+              u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[2], h[3]);
+              u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[4], h[5]);
+              u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[6], h[7]);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) h[j] = __hsub2(h[j], bias);
-          } else {
-            // (1024 + q) - (1024 + z) = q - z exactly, then one rounding in the scale product;
-            // rows past N were zero-filled by TMA (s = 0), so their weights are 0
-            const __half2 zb =
-                __half2half2(__ushort_as_half((unsigned short)(0x6400u | sb[Cfg::Z_OFF + row])));
-            const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[row]);
-            u8x4_to_h2x2_biased(x[i].x, h[0], h[1]);
-            u8x4_to_h2x2_biased(x[i].y, h[2], h[3]);
-            u8x4_to_h2x2_biased(x[i].z, h[4], h[5]);
-            u8x4_to_h2x2_biased(x[i].w, h[6], h[7]);
+              for (int j = 0; j < 8; ++j) h[j] = __hsub2(h[j], bias);
+            } else {
+              // (1024 + q) - (1024 + z) = q - z exactly, then one rounding in the scale
+              // product; rows past N were zero-filled by TMA (s = 0), so their weights are 0
+              const __half2 zb = __half2half2(
+                  __ushort_as_half((unsigned short)(0x6400u | sb[Cfg::Z_OFF + row])));
+              const __half2 s2 =
+                  __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[row]);
+              u8x4_to_h2x2_biased(x[u].x, h[0], h[1]);
+              u8x4_to_h2x2_biased(x[u].y, h[2], h[3]);
+              u8x4_to_h2x2_biased(x[u].z, h[4], h[5]);
+              u8x4_to_h2x2_biased(x[u].w, h[6], h[7]);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) h[j] = __hmul2(__hsub2(h[j], zb), s2);
+              for (int j = 0; j < 8; ++j) h[j] = __hmul2(__hsub2(h[j], zb), s2);
+            }
+            const uint4* hv = reinterpret_cast<const uint4*>(h);
+            uint8_t* drow = dst + row * 128;
+            *reinterpret_cast<uint4*>(drow + (((2 * kq) ^ (row & 7)) * 16)) = hv[0];
+            *reinterpret_cast<uint4*>(drow + (((2 * kq + 1) ^ (row & 7)) * 16)) = hv[1];
           }
-          const uint4* hv = reinterpret_cast<const uint4*>(h);
-          uint8_t* drow = dst + row * 128;
-          *reinterpret_cast<uint4*>(drow + (((2 * kq) ^ (row & 7)) * 16)) = hv[0];
-          *reinterpret_cast<uint4*>(drow + (((2 * kq + 1) ^ (row & 7)) * 16)) = hv[1];
         }
         fence_proxy_async_smem();  // generic-proxy stores -> the MMA's async-proxy reads
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(lead_deq + 8u * stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
     }
   } else {

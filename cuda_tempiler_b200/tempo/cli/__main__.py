@@ -13,7 +13,9 @@
   measure --arch sm100 -M -N -K        GPU: correctness gate, then paired timing vs cuBLAS and naive
   tune [--set fp16|w8pc|w8g|all]       GPU: measured sweep of the shipped family -> JSON
   calibrate [--device N]               GPU: probe the NOT_MEASURED channels -> tempo/calib/2 record
+  passport [--out FILE]                GPU: card state + gate over every production point
   ship --from TUNE.json                derive the M-ladder, write kernels/shipped/<op>/sm_100a
+  ship --passport FILE                 re-freeze, writing card and gate into the manifests
 
 Weights: --dtype-b fp16 (default) | int8 (per-channel scale) | uint8 (--scale group:128).
 """
@@ -217,6 +219,11 @@ def cmd_calibrate(a):
     return 0
 
 
+def cmd_passport(a):
+    from ..passport_stage import main as passport_main
+    return passport_main(a.out, a.device)
+
+
 def cmd_ship(a):
     from ..plugins.sm100 import ship
     rows = json.load(open(a.source)) if a.source else []
@@ -257,8 +264,18 @@ def cmd_ship(a):
         else:
             lad, measured = list(ship.DEFAULT_LADDER), []
         m0 = json.load(open(prev)) if os.path.exists(prev) else {}
+        gate, card = m0.get("gate"), m0.get("card")
+        if getattr(a, "passport", None):
+            pp = json.load(open(a.passport))
+            card = pp["card"]
+            g = dict(pp["gate"][op])
+            g["rows"] = [{k: r[k] for k in ("gemm", "M", "N", "K", "rel_l2", "spot_fp64",
+                                             "uncovered") if k in r} | ({"scale": r["scale"]}
+                                                                        if "scale" in r else {})
+                         for r in g["rows"]]
+            gate = g
         m = ship.write_ship(op, lad, root, build_facts=facts, measured=measured,
-                            gate=m0.get("gate"), card=m0.get("card"))
+                            gate=gate, card=card)
         print(f"shipped {op}: ladder {m['ladder']}")
     if facts:
         d = os.path.join(os.path.dirname(ship.__file__), "data", "build_facts.json")
@@ -310,7 +327,13 @@ def main(argv=None):
     s.add_argument("--device", type=int, default=0)
     s.add_argument("--out", default=None, help="record directory (default: the plugin's data/calib)")
     s.set_defaults(fn=cmd_calibrate)
+    s = sub.add_parser("passport")
+    s.add_argument("--device", type=int, default=0)
+    s.add_argument("--out", default=None)
+    s.set_defaults(fn=cmd_passport)
     s = sub.add_parser("ship")
+    s.add_argument("--passport", default=None,
+                   help="tempo/passport/1 JSON (from `passport`): card and gate into the manifests")
     s.add_argument("--from", dest="source", default=None)
     s.add_argument("--out", default=None)
     s.add_argument("--merge", action="store_true",

@@ -322,6 +322,41 @@ __device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
   }
 }
 
+// Non-blocking probe of a phase with cluster-scope acquire.  try_wait may suspend the thread
+// until a hardware time limit when the completing arrive comes from another CTA of the
+// cluster; a barrier completed by remote arrivals every k-block is polled with test_wait.
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded polling wait (test_wait) with cluster-scope acquire.
+__device__ __noinline__ bool mbar_poll_cluster(uint32_t bar, uint32_t parity,
+                                               volatile int* abort_flag, int where) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 1024; ++i)
+      if (mbar_test_wait_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      if (atomicCAS(&g_status[0], 0, 1) == 0) {
+        g_status[1] = where;
+        g_status[2] = blockIdx.x;
+      }
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
 // Stores into the shared memory of a CTA of this cluster (shared::cluster address).
 __device__ __forceinline__ void st_dsmem_f32(uint32_t cluster_addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
