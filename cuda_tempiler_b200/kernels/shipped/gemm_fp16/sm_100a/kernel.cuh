@@ -1848,65 +1848,39 @@ __device__ __forceinline__ void tile_pos(const GemmArgs& a, int tile, int& tp, i
   tq = r / gm;
 }
 
-template <int BN_, int WQ_ = 0>
+template <int BN_>
 struct PairCfg {
-  static constexpr int BM = 128, BN = BN_, BK = 64, WQ = WQ_;
+  static constexpr int BM = 128, BN = BN_, BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's fp16 B half of a k-block
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
   static constexpr int B_OFF = A_BYTES;
-  // W8A16: the raw 8-bit B half [BN/2][64] (unswizzled 64-byte rows) that the dequant warps
-  // turn into the fp16 B half, then (group-wise) the stage's scale row (fp16) and zero row
-  // (uint8) for those BN/2 weight rows
-  static constexpr int RAW_OFF = B_OFF + round_up(B_BYTES, 1024);
-  static constexpr int RAW_BYTES = WQ ? (BN / 2) * BK : 0;
-  static constexpr int S_OFF = RAW_OFF + RAW_BYTES;
-  static constexpr int Z_OFF = S_OFF + (BN / 2) * 2;
-  static constexpr int SZ_BYTES = WQ == 2 ? (BN / 2) * 3 : 0;
-  static constexpr int STAGE_BYTES =
-      WQ ? RAW_OFF + round_up(RAW_BYTES + SZ_BYTES, 1024) : A_BYTES + round_up(B_BYTES, 1024);
+  static constexpr int STAGE_BYTES = A_BYTES + round_up(B_BYTES, 1024);
   static constexpr int EPI_BYTES = 4 * 2 * 2048;
   static constexpr int BAR_BYTES = 512;
   static constexpr int STAGES = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES, 8);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
-  // W8A16: one dequant warp per stage (warps 6 .. 5 + STAGES), each owning its stage
-  static constexpr int DEQ_WARPS = WQ ? STAGES : 0;
-  static constexpr int THREADS = 192 + 32 * DEQ_WARPS;
-  // raw 16-byte chunks of a stage's B half (a multiple of 4 x 32: one warp, 4 in flight)
-  static constexpr int DEQ_CHUNKS = WQ ? RAW_BYTES / 16 : 0;
-  // barriers: full[S], empty[S], tfull[2], tempty[2], done, then (W8A16) raw[S], deq[S]
-  static constexpr int NBARS = 2 * STAGES + 5 + (WQ ? 2 * STAGES : 0);
+  static constexpr int THREADS = 192;
   // accumulator buffer b starts at TMEM column b * ACC_STRIDE (a power of two)
   static constexpr int ACC_STRIDE = BN <= 128 ? 128 : 256;
   static constexpr int TMEM_COLS = tmem_cols_for(2 * ACC_STRIDE);
   static_assert(BN % 32 == 0 && BN >= 128 && BN <= 256,
                 "pair tiles are 256 x BN, BN in 128..256 step 32 (32-column epilogue chunks)");
-  static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
-  static_assert(!WQ || DEQ_CHUNKS % 128 == 0, "dequant chunks: whole passes of 4 per lane");
-  static_assert(SMEM <= kMaxDynSmem, "shared memory");
+  static_assert(2 * STAGES + 5 <= BAR_BYTES / 8 - 2, "barrier area too small");
 };
 
-// WQ != 0 (W8A16): mapB covers the raw 8-bit weights [N][K]; each CTA's 8 dequant warps turn
-// its raw B half into the fp16 B half of the stage in shared memory (generic-proxy stores,
-// fence.proxy.async, then an arrive on the leader's deq barrier, whose count is both CTAs'
-// dequant warps), and the leader's MMA waits for A (full) and both dequantised halves (deq).
-// mapS / mapZ (group-wise) are the scale [K/g][N] fp16 and zero [K/g][N] uint8 rows; the
-// per-channel scale is applied in the epilogue.  No split tail and no SwiGLU with WQ.
-template <int BN, bool SWIGLU, int WQ = 0>
-__global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
+template <int BN, bool SWIGLU>
+__global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
     k_gemm_sm100_pair(const __grid_constant__ CUtensorMap mapA,
                       const __grid_constant__ CUtensorMap mapB,
-                      const __grid_constant__ CUtensorMap mapC,
-                      const __grid_constant__ CUtensorMap mapS,
-                      const __grid_constant__ CUtensorMap mapZ, const GemmArgs args) {
-  using Cfg = PairCfg<BN, WQ>;
-  static_assert(!(SWIGLU && WQ), "the fused SwiGLU epilogue is fp16-only");
+                      const __grid_constant__ CUtensorMap mapC, const GemmArgs args) {
+  using Cfg = PairCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* epi_smem = smem + STAGES * Cfg::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -1921,8 +1895,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
   auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
   auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
   const uint32_t done_bar = bar_base + 8u * (2 * STAGES + 4);
-  auto raw_bar = [&](int s) { return bar_base + 8u * (2 * STAGES + 5 + s); };
-  auto deq_bar = [&](int s) { return bar_base + 8u * (3 * STAGES + 5 + s); };
   auto a_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES; };
   auto b_addr = [&](int s) { return smem_base + s * Cfg::STAGE_BYTES + Cfg::B_OFF; };
 
@@ -1933,10 +1905,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);   // leader: its own arrive.expect_tx + both CTAs' bytes
       mbar_init(empty_bar(s), 1);  // multicast commit from the leader's MMA thread
-      if (WQ) {
-        mbar_init(raw_bar(s), 1);                   // this CTA's raw weight (+ scale/zero) bytes
-        mbar_init(deq_bar(s), 2);  // leader: the owning dequant warp of each CTA
-      }
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
@@ -1950,10 +1918,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapB);
     tma_prefetch_desc(&mapC);
-    if (WQ == kWUint8Group) {
-      tma_prefetch_desc(&mapS);
-      tma_prefetch_desc(&mapZ);
-    }
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -1982,26 +1946,11 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         bool ok = true;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, 11)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
           const uint32_t lead_full = mapa_shared(full_bar(stage), 0);
           const int kx = kb * Cfg::BK;
-          const int nrow = tq * BN + (int)rank * (BN / 2);
-          if (WQ == 0) {
-            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * (Cfg::A_BYTES + Cfg::B_BYTES));
-            tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
-            tma_load_2d_pair(b_addr(stage), &mapB, lead_full, kx, nrow, pol);
-          } else {
-            if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * Cfg::A_BYTES);
-            tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
-            // the raw weights (and their group's scale / zero rows) land in this CTA only
-            const uint32_t sb = a_addr(stage);
-            mbar_arrive_expect_tx(raw_bar(stage), Cfg::RAW_BYTES + Cfg::SZ_BYTES);
-            tma_load_2d(sb + Cfg::RAW_OFF, &mapB, raw_bar(stage), kx, nrow, pol);
-            if (WQ == kWUint8Group) {
-              const int g = kx / args.group_size;
-              tma_load_2d(sb + Cfg::S_OFF, &mapS, raw_bar(stage), nrow, g, pol);
-              tma_load_2d(sb + Cfg::Z_OFF, &mapZ, raw_bar(stage), nrow, g, pol);
-            }
-          }
+          tma_load_2d_pair(a_addr(stage), &mapA, lead_full, kx, tp * 256 + (int)rank * 128, pol);
+          tma_load_2d_pair(b_addr(stage), &mapB, lead_full, kx, tq * BN + (int)rank * (BN / 2), pol);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -2010,9 +1959,8 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         }
         if (!ok) break;
       }
-      // Drain: the leader's full barriers see every byte both CTAs requested; each CTA's raw
-      // barriers (W8A16) every byte of its own weight loads.
-      {
+      // Drain: the leader's full barriers see every byte both CTAs requested.
+      if (leader) {
         const int pending = issued < STAGES ? issued : STAGES;
         int s = stage;
         uint32_t ph = phase;
@@ -2021,8 +1969,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
             s = STAGES - 1;
             ph ^= 1u;
           }
-          if (leader) mbar_drain(full_bar(s), ph, 100000000ull);
-          if (WQ) mbar_drain(raw_bar(s), ph, 100000000ull);
+          mbar_drain(full_bar(s), ph, 100000000ull);
         }
       }
     }
@@ -2045,11 +1992,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         bool ok = true;
         for (int kb = kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag, 13)) { ok = false; break; }
-          if (WQ && !mbar_test_wait_cluster(deq_bar(stage), phase) &&
-              !mbar_poll_cluster(deq_bar(stage), phase, abort_flag, 18)) {
-            ok = false;
-            break;
-          }
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k)
@@ -2067,77 +2009,6 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
       }
       umma_commit_pair_mc(done_bar, 0x1);
       mbar_drain(done_bar, 0, 100000000ull);
-    }
-  } else if (WQ && warp >= 6) {
-    // ------------------------------------------------------------------ dequant (W8A16, both)
-    // Dequant warp d owns the stages s with s % DEQ_WARPS == d and converts each of them alone,
-    // so up to DEQ_WARPS stages are converted at once: the release of a stage to the leader
-    // (fence.proxy.async, then an arrive with cluster-scope release) waits for the warp's stores
-    // and takes far longer than the conversion, and owning whole stages overlaps those waits.
-    // Lane l converts raw chunks c = l + 32 i: 16 bytes = 16 weights of row c / 4, k-range
-    // 16 (c % 4); its fp16 results are the row's 16-byte granules 2 (c % 4) and 2 (c % 4) + 1,
-    // stored at granule ^ (row & 7) (the 128-byte swizzle TMA would have produced).  Reads are
-    // consecutive 16-byte chunks; each pass of stores covers every granule position of its 8
-    // rows once: no bank conflicts.
-    const int dw = warp - 6;
-    const uint32_t lead_deq = mapa_shared(deq_bar(0), 0);
-    int sit = 0;  // stage-iteration sequence number, the same sequence as the producer's
-    PairSegIter segs(args, cluster, nclusters);
-    PairSeg sg;
-    bool ok = true;
-    while (ok && segs.next(args, sg)) {
-      for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++sit) {
-        const int stage = sit % STAGES;
-        if (stage % Cfg::DEQ_WARPS != dw) continue;  // a stage always has the same owner
-        const uint32_t phase = (uint32_t)((sit / STAGES) & 1);
-        if (!mbar_wait(raw_bar(stage), phase, abort_flag, 17)) { ok = false; break; }
-        uint8_t* sb = smem + stage * Cfg::STAGE_BYTES;
-        const uint8_t* raw = sb + Cfg::RAW_OFF;
-        uint8_t* dst = sb + Cfg::B_OFF;
-#pragma unroll 1
-        for (int i0 = 0; i0 < Cfg::DEQ_CHUNKS / 32; i0 += 4) {
-          uint4 x[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            x[u] = *reinterpret_cast<const uint4*>(raw + (lane + 32 * (i0 + u)) * 16);
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int c = lane + 32 * (i0 + u);
-            const int row = c >> 2, kq = c & 3;
-            __half2 h[8];
-            if (WQ == kWInt8PerChannel) {
-              // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
-              const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
-              u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[0], h[1]);
-              u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[2], h[3]);
-              u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[4], h[5]);
-              u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[6], h[7]);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) h[j] = __hsub2(h[j], bias);
-            } else {
-              // (1024 + q) - (1024 + z) = q - z exactly, then one rounding in the scale
-              // product; rows past N were zero-filled by TMA (s = 0), so their weights are 0
-              const __half2 zb = __half2half2(
-                  __ushort_as_half((unsigned short)(0x6400u | sb[Cfg::Z_OFF + row])));
-              const __half2 s2 =
-                  __half2half2(reinterpret_cast<const __half*>(sb + Cfg::S_OFF)[row]);
-              u8x4_to_h2x2_biased(x[u].x, h[0], h[1]);
-              u8x4_to_h2x2_biased(x[u].y, h[2], h[3]);
-              u8x4_to_h2x2_biased(x[u].z, h[4], h[5]);
-              u8x4_to_h2x2_biased(x[u].w, h[6], h[7]);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) h[j] = __hmul2(__hsub2(h[j], zb), s2);
-            }
-            const uint4* hv = reinterpret_cast<const uint4*>(h);
-            uint8_t* drow = dst + row * 128;
-            *reinterpret_cast<uint4*>(drow + (((2 * kq) ^ (row & 7)) * 16)) = hv[0];
-            *reinterpret_cast<uint4*>(drow + (((2 * kq + 1) ^ (row & 7)) * 16)) = hv[1];
-          }
-        }
-        fence_proxy_async_smem();  // generic-proxy stores -> the MMA's async-proxy reads
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(lead_deq + 8u * stage);
-      }
     }
   } else {
     // ------------------------------------------------------------------ epilogue (both)
@@ -2169,7 +2040,7 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
         continue;
       }
-      if (WQ == 0 && sg.contrib > 1) {
+      if (sg.contrib > 1) {
         // Tail k-slice: this CTA's 128 x BN fp32 partial goes to slot (slice, t), laid out
         // [32-column chunk][row][32] so each thread writes and reads its row's 128 contiguous
         // bytes per chunk as float4s.  The last of the tile's k-slices to arrive keeps its own
@@ -2315,6 +2186,372 @@ __global__ void __launch_bounds__(PairCfg<BN, WQ>::THREADS, 1)
         }
         continue;
       }
+      const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
+#pragma unroll 1
+      for (int c = 0; c < nchunk; ++c) {
+        float f[32];
+        acc_chunk<32, 1, BN>(t_acc, c, f);
+        if (c == nchunk - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+        }
+        if (!rows_live) continue;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        uint8_t* sbuf = stage_buf + sb * 2048;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          w.x = pack_half2(f[8 * g + 0], f[8 * g + 1]);
+          w.y = pack_half2(f[8 * g + 2], f[8 * g + 3]);
+          w.z = pack_half2(f[8 * g + 4], f[8 * g + 5]);
+          w.w = pack_half2(f[8 * g + 6], f[8 * g + 7]);
+          const int pg = g ^ ((lane >> 1) & 3);  // 64-byte swizzle
+          *reinterpret_cast<uint4*>(sbuf + lane * 64 + pg * 16) = w;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&mapC, smem_u32(sbuf), q0 + c * 32, row0);
+          bulk_commit_group();
+        }
+        sb ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers or smem
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// k_gemm_sm100_pair_w8: W8A16 prefill tiles of 256 x BN on a 2-CTA cluster (cta_group::2).
+//
+// The fp16 pair kernel's shape (CTA r holds A rows [256 t + 128 r, +128) and weight rows
+// [BN u + (BN/2) r, +BN/2); the leader issues tcgen05.mma.cta_group::2), with the weights read
+// as 8 bits and dequantised to fp16 in shared memory by each CTA for its own half.  Each of the
+// NS slots holds an MMA part [A 128 x 64 fp16 | B half (BN/2) x 64 fp16, 128-byte swizzle] and a
+// raw part [raw B half (BN/2) x 64 bytes | group-wise scale row | zero row].  The raw part is
+// released (and refilled by warp 6) as soon as its dequant warps have read it, well before the
+// MMA frees the slot's MMA part, so the weights' HBM latency hides behind the conversions and
+// MMAs of the other slots.  A slot's MMA part: the MMA reading it completes (commit multicast:
+// empty) -> warp 0 refills its A (the leader's full barrier counts both CTAs' bytes) while the
+// slot's dequant warps convert its raw part into the B half, fence the generic-proxy stores for
+// the async proxy and arrive on the leader's deq barrier -> the leader's MMA waits for full and
+// deq.  Measured on B200 (clock64 trace of one stage): raw TMA latency 1000-3000 cycles, one
+// warp converting 8192 weights ~700-1100 cycles, the arrive with cluster-scope release
+// 1000-2000 cycles: every slot has its own dequant warps, so these overlap across slots.
+//
+// Warps: 0 A producer, 1 MMA issuer (leader) / TMEM owner, 2-5 epilogue, 6 raw producer,
+// 7 .. 6 + NS * WPG dequant (WPG warps own each slot, so every wait on a slot's barriers is
+// made by its single owner group, in order, and never sees an older phase).  Per-channel scales
+// are applied in the epilogue; group-wise scale and zero point in the dequant.  Whole tiles
+// only (no split tail), no SwiGLU.
+// ---------------------------------------------------------------------------------------------
+template <int BN_>
+struct PairW8Cfg {
+  static constexpr int BM = 128, BN = BN_, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int X_BYTES = A_BYTES + round_up(B_BYTES, 1024);  // a slot's MMA part
+  static constexpr int RAW_BYTES = (BN / 2) * BK;
+  static constexpr int S_OFF = RAW_BYTES;                   // group-wise scale row (fp16)
+  static constexpr int Z_OFF = RAW_BYTES + (BN / 2) * 2;    // group-wise zero row (uint8)
+  static constexpr int SZ_BYTES = (BN / 2) * 3;
+  static constexpr int R_BYTES = round_up(RAW_BYTES + SZ_BYTES, 1024);  // a slot's raw part
+  static constexpr int EPI_BYTES = 4 * 2 * 2048;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int NS = cmin((kMaxDynSmem - 1024 - EPI_BYTES - BAR_BYTES) / (X_BYTES + R_BYTES), 8);
+  static constexpr int SMEM = 1024 + NS * (X_BYTES + R_BYTES) + EPI_BYTES + BAR_BYTES;
+  static constexpr int WPG = BN / 128;  // dequant warps per slot: 256 raw chunks each
+  static constexpr int DEQ_WARPS = NS * WPG;
+  static constexpr int THREADS = 32 * (7 + DEQ_WARPS);
+  static constexpr int CHUNKS_PER_WARP = RAW_BYTES / 16 / WPG;
+  static constexpr int NBARS = 5 * NS + 5;
+  static constexpr int ACC_STRIDE = BN <= 128 ? 128 : 256;
+  static constexpr int TMEM_COLS = tmem_cols_for(2 * ACC_STRIDE);
+  static_assert(BN == 128 || BN == 256, "W8A16 pair tiles are 256 x 128 or 256 x 256");
+  static_assert(NS >= 2, "at least two slots");
+  static_assert(NBARS <= BAR_BYTES / 8 - 2, "barrier area too small");
+  static_assert(CHUNKS_PER_WARP % 128 == 0, "dequant: whole passes of 4 chunks per lane");
+  static_assert(SMEM <= kMaxDynSmem, "shared memory");
+};
+
+template <int BN, int WQ>
+__global__ void __launch_bounds__(PairW8Cfg<BN>::THREADS, 1)
+    k_gemm_sm100_pair_w8(const __grid_constant__ CUtensorMap mapA,
+                         const __grid_constant__ CUtensorMap mapW,
+                         const __grid_constant__ CUtensorMap mapC,
+                         const __grid_constant__ CUtensorMap mapS,
+                         const __grid_constant__ CUtensorMap mapZ, const GemmArgs args) {
+  using Cfg = PairW8Cfg<BN>;
+  constexpr int NS = Cfg::NS;
+  static_assert(WQ == kWInt8PerChannel || WQ == kWUint8Group, "8-bit weights");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* raw_smem = smem + NS * Cfg::X_BYTES;
+  uint8_t* epi_smem = raw_smem + NS * Cfg::R_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t bar_base = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (NS + s); };
+  auto deq_bar = [&](int s) { return bar_base + 8u * (2 * NS + s); };
+  auto rfull_bar = [&](int s) { return bar_base + 8u * (3 * NS + s); };
+  auto rempty_bar = [&](int s) { return bar_base + 8u * (4 * NS + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (5 * NS + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (5 * NS + 2 + b); };
+  const uint32_t done_bar = bar_base + 8u * (5 * NS + 4);
+  auto a_addr = [&](int s) { return smem_base + s * Cfg::X_BYTES; };
+  auto b_addr = [&](int s) { return smem_base + s * Cfg::X_BYTES + Cfg::A_BYTES; };
+  auto r_addr = [&](int s) { return smem_u32(raw_smem) + s * Cfg::R_BYTES; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(full_bar(s), 1);              // leader: both CTAs' A bytes
+      mbar_init(empty_bar(s), 1);             // multicast commit from the leader's MMA thread
+      mbar_init(deq_bar(s), 2 * Cfg::WPG);    // leader: the slot's dequant warps of both CTAs
+      mbar_init(rfull_bar(s), 1);             // this CTA's raw (+ scale / zero) bytes
+      mbar_init(rempty_bar(s), Cfg::WPG);     // this CTA's dequant warps done reading them
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 8);            // leader: 4 epilogue warps of each CTA
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapC);
+  }
+  if (warp == 6 && lane == 0) {
+    tma_prefetch_desc(&mapW);
+    if (WQ == kWUint8Group) {
+      tma_prefetch_desc(&mapS);
+      tma_prefetch_desc(&mapZ);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ A producer (both)
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int it = 0;
+      PairSegIter segs(args, cluster, nclusters);
+      PairSeg sg;
+      bool ok = true;
+      while (ok && segs.next(args, sg)) {
+        int tp, tq;
+        tile_pos(args, sg.tile, tp, tq);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = (uint32_t)((it / NS) & 1);
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, 11)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::A_BYTES);
+          tma_load_2d_pair(a_addr(s), &mapA, mapa_shared(full_bar(s), 0), kb * Cfg::BK,
+                           tp * 256 + (int)rank * 128, pol);
+        }
+      }
+      if (leader) {  // the leader's full barriers see every A byte both CTAs requested
+        const int pending = it < NS ? it : NS;
+        for (int j = it - pending; j < it; ++j)
+          mbar_drain(full_bar(j % NS), (uint32_t)((j / NS) & 1), 100000000ull);
+      }
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------------ raw producer (both)
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      int it = 0;
+      PairSegIter segs(args, cluster, nclusters);
+      PairSeg sg;
+      bool ok = true;
+      while (ok && segs.next(args, sg)) {
+        int tp, tq;
+        tile_pos(args, sg.tile, tp, tq);
+        const int nrow = tq * BN + (int)rank * (BN / 2);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = (uint32_t)((it / NS) & 1);
+          if (!mbar_wait(rempty_bar(s), ph ^ 1u, abort_flag, 19)) { ok = false; break; }
+          mbar_arrive_expect_tx(rfull_bar(s),
+                                Cfg::RAW_BYTES + (WQ == kWUint8Group ? Cfg::SZ_BYTES : 0));
+          const int kx = kb * Cfg::BK;
+          tma_load_2d(r_addr(s), &mapW, rfull_bar(s), kx, nrow, pol);
+          if (WQ == kWUint8Group) {
+            const int g = kx / args.group_size;
+            tma_load_2d(r_addr(s) + Cfg::S_OFF, &mapS, rfull_bar(s), nrow, g, pol);
+            tma_load_2d(r_addr(s) + Cfg::Z_OFF, &mapZ, rfull_bar(s), nrow, g, pol);
+          }
+        }
+      }
+      const int pending = it < NS ? it : NS;  // every raw byte landed before the CTA exits
+      for (int j = it - pending; j < it; ++j)
+        mbar_drain(rfull_bar(j % NS), (uint32_t)((j / NS) & 1), 100000000ull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(256, BN);
+      int it = 0;
+      int lu = 0;
+      PairSegIter segs(args, cluster, nclusters);
+      PairSeg sg;
+      for (; segs.next(args, sg); ++lu) {
+        const int buf = lu & 1;
+        const uint32_t uphase = (lu >> 1) & 1;
+        if (!mbar_wait_cluster(tempty_bar(buf), uphase ^ 1u, abort_flag, 12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * Cfg::ACC_STRIDE;
+        bool ok = true;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = (uint32_t)((it / NS) & 1);
+          if (!mbar_wait(full_bar(s), ph, abort_flag, 13)) { ok = false; break; }
+          if (!mbar_test_wait_cluster(deq_bar(s), ph) &&
+              !mbar_poll_cluster(deq_bar(s), ph, abort_flag, 18)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k)
+            umma_f16_ss_pair(d_tmem, sdesc_k_sw128(a_addr(s) + k * 32),
+                             sdesc_k_sw128(b_addr(s) + k * 32), idesc,
+                             (kb > sg.kb0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_mc(empty_bar(s), 0x3);
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(tfull_bar(buf), 0x3);
+      }
+      umma_commit_pair_mc(done_bar, 0x1);
+      mbar_drain(done_bar, 0, 100000000ull);
+    }
+  } else if (warp >= 7) {
+    // ------------------------------------------------------------------ dequant (both)
+    // Group g = (warp - 7) / WPG owns slot g, hence every iteration it with it % NS == g.
+    // Warp w of the group converts raw chunks [w, w + 1) x CHUNKS_PER_WARP: chunk c is 16
+    // weights of row c / 4, k-range 16 (c % 4); lane l takes c = l + 32 i, so reads are
+    // consecutive 16-byte chunks, and the row's two fp16 granules 2 (c % 4), 2 (c % 4) + 1 go
+    // to granule ^ (row & 7), the 128-byte swizzle of the MMA operand (each pass of stores hits
+    // every granule position of its 8 rows once: no bank conflicts).
+    const int dw = warp - 7;
+    const int grp = dw / Cfg::WPG;
+    const int c0 = (dw % Cfg::WPG) * Cfg::CHUNKS_PER_WARP;
+    const uint32_t lead_deq = mapa_shared(deq_bar(grp), 0);
+    const uint8_t* raw = raw_smem + grp * Cfg::R_BYTES;
+    uint8_t* dst = smem + grp * Cfg::X_BYTES + Cfg::A_BYTES;
+    int it = 0;
+    PairSegIter segs(args, cluster, nclusters);
+    PairSeg sg;
+    bool ok = true;
+    while (ok && segs.next(args, sg)) {
+      for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
+        if (it % NS != grp) continue;
+        const uint32_t ph = (uint32_t)((it / NS) & 1);
+        if (!mbar_wait(rfull_bar(grp), ph, abort_flag, 17) ||
+            !mbar_wait(empty_bar(grp), ph ^ 1u, abort_flag, 20)) {
+          ok = false;
+          break;
+        }
+#pragma unroll 1
+        for (int i0 = 0; i0 < Cfg::CHUNKS_PER_WARP / 32; i0 += 4) {
+          uint4 x[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            x[u] = *reinterpret_cast<const uint4*>(raw + (c0 + lane + 32 * (i0 + u)) * 16);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int c = c0 + lane + 32 * (i0 + u);
+            const int row = c >> 2, kq = c & 3;
+            __half2 h[8];
+            if (WQ == kWInt8PerChannel) {
+              // signed byte b -> (b ^ 0x80) = b + 128; 1024 + (b + 128) - 1152 = b, exact
+              const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+              u8x4_to_h2x2_biased(x[u].x ^ 0x80808080u, h[0], h[1]);
+              u8x4_to_h2x2_biased(x[u].y ^ 0x80808080u, h[2], h[3]);
+              u8x4_to_h2x2_biased(x[u].z ^ 0x80808080u, h[4], h[5]);
+              u8x4_to_h2x2_biased(x[u].w ^ 0x80808080u, h[6], h[7]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) h[j] = __hsub2(h[j], bias);
+            } else {
+              // (1024 + q) - (1024 + z) = q - z exactly, then one rounding in the scale
+              // product; rows past N were zero-filled by TMA (s = 0), so their weights are 0
+              const __half2 zb = __half2half2(
+                  __ushort_as_half((unsigned short)(0x6400u | raw[Cfg::Z_OFF + row])));
+              const __half2 s2 =
+                  __half2half2(reinterpret_cast<const __half*>(raw + Cfg::S_OFF)[row]);
+              u8x4_to_h2x2_biased(x[u].x, h[0], h[1]);
+              u8x4_to_h2x2_biased(x[u].y, h[2], h[3]);
+              u8x4_to_h2x2_biased(x[u].z, h[4], h[5]);
+              u8x4_to_h2x2_biased(x[u].w, h[6], h[7]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) h[j] = __hmul2(__hsub2(h[j], zb), s2);
+            }
+            const uint4* hv = reinterpret_cast<const uint4*>(h);
+            uint8_t* drow = dst + row * 128;
+            *reinterpret_cast<uint4*>(drow + (((2 * kq) ^ (row & 7)) * 16)) = hv[0];
+            *reinterpret_cast<uint4*>(drow + (((2 * kq + 1) ^ (row & 7)) * 16)) = hv[1];
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(rempty_bar(grp));  // raw part read: the producer may refill
+        fence_proxy_async_smem();  // generic-proxy stores -> the MMA's async-proxy reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_deq);  // this half of the B operand is ready
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both)
+    const int quad = warp & 3;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quad * 32) << 16);
+    uint8_t* stage_buf = epi_smem + (warp - 2) * 4096;
+    int sb = 0;
+    int lu = 0;
+    PairSegIter segs(args, cluster, nclusters);
+    PairSeg sg;
+    for (; segs.next(args, sg); ++lu) {
+      int tp, tq;
+      tile_pos(args, sg.tile, tp, tq);
+      const int buf = lu & 1;
+      const uint32_t uphase = (lu >> 1) & 1;
+      if (!mbar_wait(tfull_bar(buf), uphase, abort_flag, 14)) break;
+      tc_fence_after();
+      const uint32_t t_acc = t_lane + buf * Cfg::ACC_STRIDE;
+      const int q0 = tq * BN;
+      const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
+      const int live_cols = args.rows_q - q0;
+      const bool rows_live = row0 < args.rows_p;
       const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;
 #pragma unroll 1
       for (int c = 0; c < nchunk; ++c) {

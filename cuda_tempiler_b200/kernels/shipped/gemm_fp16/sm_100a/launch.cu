@@ -532,10 +532,70 @@ PairPlan pair_plan(int M, int N, int K, int bn, int sms, int max_ctas, bool spli
 
 // 2-CTA (cta_group::2) fp16 prefill launch: persistent clusters of two CTAs; h.splits > 1
 // allows the split tail of pair_plan.
-template <int BN, bool SWIGLU = false, int WQ = 0>
+template <int BN, bool SWIGLU = false>
 cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
-  using Cfg = PairCfg<BN, WQ>;
-  auto kern = k_gemm_sm100_pair<BN, SWIGLU, WQ>;
+  using Cfg = PairCfg<BN>;
+  auto kern = k_gemm_sm100_pair<BN, SWIGLU>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t attr_err[kMaxDevices];
+    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [&] {
+      attr_err[dev] =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    });
+    if (attr_err[dev] != cudaSuccess) return attr_err[dev];
+  }
+  if (pr.wkind != 0 || h.swap) return cudaErrorInvalidConfiguration;
+  if (SWIGLU && (pr.N % 128 || (BN != 128 && BN != 256))) return cudaErrorInvalidConfiguration;
+  // the fused SwiGLU epilogue has no split tail (its partial sums would be pre-activation)
+  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas,
+                                !SWIGLU && h.splits > 1,
+                                pr.ws ? pr.ws_bytes : 0);
+  GemmArgs a{};
+  a.rows_p = pr.M;
+  a.rows_q = pr.N;
+  a.K = pr.K;
+  a.tiles_p = (pr.M + 255) / 256;
+  a.tiles_q = (pr.N + BN - 1) / BN;
+  a.num_kb = (pr.K + Cfg::BK - 1) / Cfg::BK;
+  a.splits = 1;
+  a.num_units = a.tiles_p * a.tiles_q;
+  a.group_m = std::max(1, h.group_m / 2);  // raster groups counted in 256-row tiles
+  a.C = static_cast<__half*>(pr.C);
+  a.ldc = pr.ldc;
+  a.weight_rows = pr.N;
+  a.sk_tile0 = pl.sk_tile0;
+  a.sk_tiles = pl.sk_tiles;
+  a.sk_splits = pl.sk_splits;
+  if (pl.sk_splits > 0) {
+    if (!pr.ws || pr.ws_bytes < pl.ws_bytes) return cudaErrorInvalidValue;
+    a.counters = static_cast<int*>(pr.ws);
+    a.ws = reinterpret_cast<float*>(pr.ws_parts ? static_cast<char*>(pr.ws_parts)
+                                                : static_cast<char*>(pr.ws) + kCounterBytes);
+  }
+  CUtensorMap mA, mB, mC;
+  std::memset(&mA, 0, sizeof(mA));
+  std::memset(&mB, 0, sizeof(mB));
+  std::memset(&mC, 0, sizeof(mC));
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  bool ok = make_map(&mA, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+  ok &= make_map(&mC, pr.C, F16, 2, SWIGLU ? pr.N / 2 : pr.N, pr.M, pr.ldc, 32, 32,
+                 CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok) return cudaErrorInvalidValue;
+  return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mB, mC,
+                   a);
+}
+
+// W8A16 2-CTA launch (k_gemm_sm100_pair_w8): whole tiles, persistent clusters.
+template <int BN, int WQ>
+cudaError_t launch_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
+  using Cfg = PairW8Cfg<BN>;
+  auto kern = k_gemm_sm100_pair_w8<BN, WQ>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -550,14 +610,9 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
   }
   if (pr.wkind != WQ || h.swap) return cudaErrorInvalidConfiguration;
-  if (SWIGLU && (pr.N % 128 || (BN != 128 && BN != 256))) return cudaErrorInvalidConfiguration;
-  if (WQ == kWUint8Group && (pr.group <= 0 || pr.group % Cfg::BK || pr.K % pr.group))
+  if (WQ == kWUint8Group && (pr.group <= 0 || pr.group % Cfg::BK || pr.K % pr.group || pr.N % 16))
     return cudaErrorInvalidConfiguration;
-  // the fused SwiGLU epilogue has no split tail (its partial sums would be pre-activation), nor
-  // has W8A16 (its per-channel scale is applied in the whole tile's epilogue)
-  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas,
-                                !SWIGLU && WQ == 0 && h.splits > 1,
-                                pr.ws ? pr.ws_bytes : 0);
+  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas, false, 0);
   GemmArgs a{};
   a.rows_p = pr.M;
   a.rows_q = pr.N;
@@ -575,39 +630,26 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.zero = static_cast<const uint8_t*>(pr.zero);
   a.group_size = pr.group > 0 ? pr.group : 1;
   a.groups_per_row = pr.group > 0 ? pr.K / pr.group : 1;
-  a.sk_tile0 = pl.sk_tile0;
-  a.sk_tiles = pl.sk_tiles;
-  a.sk_splits = pl.sk_splits;
-  if (pl.sk_splits > 0) {
-    if (!pr.ws || pr.ws_bytes < pl.ws_bytes) return cudaErrorInvalidValue;
-    a.counters = static_cast<int*>(pr.ws);
-    a.ws = reinterpret_cast<float*>(pr.ws_parts ? static_cast<char*>(pr.ws_parts)
-                                                : static_cast<char*>(pr.ws) + kCounterBytes);
-  }
-  CUtensorMap mA, mB, mC, mS, mZ;
+  a.sk_tile0 = pl.sk_tile0;  // == tiles: no split tail
+  CUtensorMap mA, mW, mC, mS, mZ;
   std::memset(&mA, 0, sizeof(mA));
-  std::memset(&mB, 0, sizeof(mB));
+  std::memset(&mW, 0, sizeof(mW));
   std::memset(&mC, 0, sizeof(mC));
   std::memset(&mS, 0, sizeof(mS));
   std::memset(&mZ, 0, sizeof(mZ));
   const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok = make_map(&mA, pr.A, F16, 2, pr.K, pr.M, pr.lda, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (WQ == 0) {
-    ok &= make_map(&mB, pr.W, F16, 2, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
-  } else {
-    // raw weights: rows of 64 bytes, unswizzled (the dequant warps apply the swizzle)
-    ok &= make_map(&mB, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (WQ == kWUint8Group) {
-      const int ng = pr.K / pr.group;
-      ok &= make_map(&mS, pr.scale, F16, 2, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
-      ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
-    }
+  // raw weights: rows of 64 bytes, unswizzled (the dequant warps apply the MMA's swizzle)
+  ok &= make_map(&mW, pr.W, U8, 1, pr.K, pr.N, pr.ldw, 64, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (WQ == kWUint8Group) {
+    const int ng = pr.K / pr.group;
+    ok &= make_map(&mS, pr.scale, F16, 2, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&mZ, pr.zero, U8, 1, pr.N, ng, pr.N, BN / 2, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   }
-  ok &= make_map(&mC, pr.C, F16, 2, SWIGLU ? pr.N / 2 : pr.N, pr.M, pr.ldc, 32, 32,
-                 CU_TENSOR_MAP_SWIZZLE_64B);
+  ok &= make_map(&mC, pr.C, F16, 2, pr.N, pr.M, pr.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return cudaErrorInvalidValue;
-  return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mB, mC,
+  return launch_ex(kern, dim3(2 * pl.clusters), dim3(Cfg::THREADS), Cfg::SMEM, st, 2, mA, mW, mC,
                    mS, mZ, a);
 }
 
@@ -630,8 +672,8 @@ cudaError_t run_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
   const bool pc = pr.wkind == kWInt8PerChannel;
   if (!pc && pr.wkind != kWUint8Group) return cudaErrorInvalidConfiguration;
   switch (h.bn) {
-    case 256: return pc ? launch_pair<256, false, 1>(pr, h, st) : launch_pair<256, false, 2>(pr, h, st);
-    case 128: return pc ? launch_pair<128, false, 1>(pr, h, st) : launch_pair<128, false, 2>(pr, h, st);
+    case 256: return pc ? launch_pair_w8<256, 1>(pr, h, st) : launch_pair_w8<256, 2>(pr, h, st);
+    case 128: return pc ? launch_pair_w8<128, 1>(pr, h, st) : launch_pair_w8<128, 2>(pr, h, st);
     default: return cudaErrorInvalidConfiguration;
   }
 }

@@ -63,7 +63,7 @@ int tempo_sm100_gemm_fp16(const void* A, const void* B, void* C, int M, int N, i
 int tempo_sm100_gemm_w8a16_applicable(const void* A, const void* W, const void* scale,
                                       const void* zero, const void* C, int M, int N, int K,
                                       int lda, int ldw, int ldc, int quant_kind, int group_size);
-/* From M = 512 on, given a workspace of at least 65536 + N * K * 2 bytes
+/* From M = 1024 on, given a workspace of at least 65536 + N * K * 2 bytes
  * (tempo_sm100_workspace_bytes asks for it), the weights are first expanded to fp16 in the
  * workspace by an HBM-bound pass and the fp16 2-CTA kernel runs on the copy; below that, or
  * with less workspace, the 8-bit weights are dequantised inside the tensor-core kernel (or the streaming GEMV for M <= 16). */

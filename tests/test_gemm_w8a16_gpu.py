@@ -160,11 +160,11 @@ def test_gemv_variants_agree_and_repeat(dev):
     assert O.rel_l2(outs[2], ref) <= TOL
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 1040, 2048), (1000, 2064, 1024), (2048, 5120, 5120)])
+@pytest.mark.parametrize("M,N,K", [(1024, 1040, 2048), (1100, 2064, 1024), (2048, 5120, 5120)])
 def test_expand_path_prefill(dev, M, N, K):
-    """M >= 512 with a full workspace: the weights are expanded to fp16 in the workspace and
+    """M >= 1024 with a full workspace: the weights are expanded to fp16 in the workspace and
     the 2-CTA fp16 kernel runs on the copy (per-channel and group-wise); without workspace the
-    same call takes the in-kernel dequant path.  Both pass the gate."""
+    same call takes the in-kernel dequant path (the W8A16 2-CTA tiles).  Both pass the gate."""
     from cuda_tempiler_b200 import ops
     sel = ops.select(1, M, N, K)
     assert sel["bn"] >= 128 and sel["swap"] == 0  # the fp16 2-CTA launch reports itself
