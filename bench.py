@@ -299,8 +299,72 @@ def tp_mlp_block(dev, world, rank, barrier):
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
+        # the same forward captured in a CUDA graph (NCCL all-reduce inside), and the all-reduce
+        # of the [M, H] partial on its own, both timed the same way
+        us_graph = us_ar = us_peer = None
+        try:
+            t_cap = time.perf_counter()
+            mg = tp.MLPGraph(sh, M, H, dev, all_reduce=ar)
+            print(f"tp={world} M={M}: graph captured in {time.perf_counter() - t_cap:.1f} s",
+                  file=sys.stderr)
+            for _ in range(3):
+                mg(x)
+            torch.cuda.synchronize()
+            barrier()
+            e0.record()
+            for _ in range(reps):
+                mg.graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            gms = e0.elapsed_time(e1) / reps
+            if world > 1:
+                t = torch.tensor([gms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                gms = float(t.item())
+                part = torch.randn(M, H, generator=g, device=dev).half()
+                for _ in range(3):
+                    dist.all_reduce(part)
+                torch.cuda.synchronize()
+                barrier()
+                e0.record()
+                for _ in range(reps):
+                    dist.all_reduce(part)
+                e1.record()
+                torch.cuda.synchronize()
+                t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                us_ar = round(float(t.item()) * 1e3, 1)
+                if par is not None and M <= 16:
+                    # the peer one-shot all-reduce of the same partial, in a graph of `reps`
+                    pg = torch.cuda.CUDAGraph()
+                    ps = torch.cuda.Stream(dev)
+                    ps.wait_stream(torch.cuda.current_stream(dev))
+                    with torch.cuda.stream(ps):
+                        par(part)
+                    ps.synchronize()
+                    with torch.cuda.graph(pg, stream=ps):
+                        for _ in range(reps):
+                            par(part)
+                    pg.replay()
+                    torch.cuda.synchronize()
+                    barrier()
+                    e0.record()
+                    pg.replay()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    us_peer = round(float(t.item()) * 1e3, 1)
+            us_graph = round(gms * 1e3, 1)
+            del mg
+            torch.cuda.synchronize()
+        except Exception as ex:  # reported beside the eager number
+            print(f"graph capture of the MLP at M={M} failed: {ex}", file=sys.stderr)
         fl = 6.0 * M * H * I
-        rows.append({"M": M, "tp": world, "us": round(ms * 1e3, 1),
+        best_ms = min(ms, us_graph / 1e3) if us_graph else ms
+        rows.append({"M": M, "tp": world, "us": round(ms * 1e3, 1), "us_graph": us_graph,
+                     "nccl_allreduce_us": us_ar, "peer_allreduce_us": us_peer,
+                     "tflops_best": round(fl / (best_ms * 1e-3) / 1e12, 1),
                      "exchange": "peer one-shot" if ar is par and par is not None else
                                  ("nccl" if world > 1 else "none"),
                      "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
@@ -754,8 +818,11 @@ def main():
     os.dup2(real_stdout, 1)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    t_end0 = time.perf_counter()
     if world > 1:
         dist.destroy_process_group()
+    print(f"rank {rank}: process group closed in {time.perf_counter() - t_end0:.1f} s",
+          file=sys.stderr, flush=True)
     return 0
 
 

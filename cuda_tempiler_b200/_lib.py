@@ -56,6 +56,9 @@ EXPORTS = {
     "tempo_sm100_allreduce_oneshot": (
         _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
              _i, _i, C.c_uint, _i, _vp]),
+    "tempo_sm100_allreduce_oneshot_dev": (
+        _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+             _i, _i, _vp, _i, _vp]),
     "tempo_sm100_allreduce_oneshot_timed": (
         _i, [_vp, _vp, C.c_longlong, C.c_longlong, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
              _i, _i, C.c_uint, _i, C.c_ulonglong, _vp]),

@@ -5,7 +5,8 @@
 // Every rank owns a receive buffer [2][tp][cap] fp16 (two halves alternate by call parity) and
 // a flag array [tp][kArMaxCtas] uint32, both mapped into every peer.  CTA b of rank r:
 //   1. stores its slice of r's vector into slot r of every rank's receive buffer (peer stores);
-//   2. fences at system scope and writes `epoch` into flag [r][b] of every rank;
+//   2. after a CTA barrier, writes `epoch` into flag [r][b] of every rank with a system-scope
+//      release store;
 //   3. waits (bounded) until flag [s][b] of its own array reads `epoch` for every rank s;
 //   4. sums slots 0 .. tp-1 of its slice in rank order (the same order on every rank, so all
 //      ranks hold bit-identical results) and writes the output.
@@ -44,8 +45,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __global__ void __launch_bounds__(256)
     k_allreduce_oneshot(const __half* src, __half* dst, long long n, long long cap,
                         const __grid_constant__ PeerSet peers, int tp, int rank, uint32_t epoch,
-                        unsigned long long wait_ns) {
+                        unsigned long long wait_ns, uint32_t* dev_epoch) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // src comes from the preceding GEMM
+  // Device-side epoch (dev_epoch != nullptr): [0] the last completed epoch, [1] CTAs done with
+  // the current call.  Every CTA reads [0] before it arrives on [1], and only the last CTA to
+  // arrive advances [0], so all CTAs of a call use the same epoch, and a call captured in a
+  // CUDA graph gets a new epoch on every replay.
+  if (dev_epoch) epoch = *reinterpret_cast<volatile uint32_t*>(dev_epoch) + 1u;
   const long long nv = n / 8;  // 16-byte vectors
   const long long per = (nv + gridDim.x - 1) / gridDim.x;
   const long long v0 = (long long)blockIdx.x * per;
@@ -57,7 +63,8 @@ __global__ void __launch_bounds__(256)
     uint4* d = reinterpret_cast<uint4*>(peers.recv[p] + half_off + (long long)rank * cap);
     for (long long v = v0 + threadIdx.x; v < v1; v += blockDim.x) d[v] = s[v];
   }
-  __threadfence_system();
+  // the CTA barrier orders every thread's slot stores before the flag stores below, and a
+  // release store is cumulative: a peer that acquires the flag sees the whole slice
   __syncthreads();
   // 2. announce it
   if (threadIdx.x < tp)
@@ -98,6 +105,17 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 4; ++j) rh[j] = __floats2half2_rn(acc[2 * j], acc[2 * j + 1]);
     o[v] = r;
+  }
+  if (dev_epoch) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(dev_epoch + 1, 1u) == gridDim.x - 1) {
+        dev_epoch[1] = 0;
+        __threadfence();
+        atomicExch(dev_epoch, epoch);
+      }
+    }
   }
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

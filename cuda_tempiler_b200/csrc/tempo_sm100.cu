@@ -284,7 +284,30 @@ int tempo_sm100_allreduce_oneshot_timed(const void* src, void* dst, long long n,
   }
   return launch_ex(k_allreduce_oneshot, dim3(ctas), dim3(256), 0,
                    static_cast<cudaStream_t>(stream), 1, static_cast<const __half*>(src),
-                   static_cast<__half*>(dst), n, cap, ps, tp, rank, (uint32_t)epoch, wait_ns);
+                   static_cast<__half*>(dst), n, cap, ps, tp, rank, (uint32_t)epoch, wait_ns,
+                   static_cast<uint32_t*>(nullptr));
+}
+
+int tempo_sm100_allreduce_oneshot_dev(const void* src, void* dst, long long n, long long cap,
+                                      void* const* recv, void* const* flags, int tp, int rank,
+                                      void* epoch_ctr, int ctas, void* stream) {
+  if (!src || !dst || !recv || !flags || !epoch_ctr || tp < 1 || tp > kArMaxTp || rank < 0 ||
+      rank >= tp)
+    return cudaErrorInvalidValue;
+  if (n <= 0 || (n % 8) || n > cap || (cap % 8) || ctas < 1 || ctas > kArMaxCtas)
+    return cudaErrorInvalidValue;
+  if (!aligned16(src) || !aligned16(dst) || (reinterpret_cast<uintptr_t>(epoch_ctr) & 7u))
+    return cudaErrorInvalidValue;
+  PeerSet ps{};
+  for (int p = 0; p < tp; ++p) {
+    if (!recv[p] || !flags[p] || !aligned16(recv[p])) return cudaErrorInvalidValue;
+    ps.recv[p] = static_cast<__half*>(recv[p]);
+    ps.flags[p] = static_cast<uint32_t*>(flags[p]);
+  }
+  return launch_ex(k_allreduce_oneshot, dim3(ctas), dim3(256), 0,
+                   static_cast<cudaStream_t>(stream), 1, static_cast<const __half*>(src),
+                   static_cast<__half*>(dst), n, cap, ps, tp, rank, 0u, kWaitLimitNs,
+                   static_cast<uint32_t*>(epoch_ctr));
 }
 
 int tempo_sm100_allreduce_oneshot(const void* src, void* dst, long long n, long long cap,

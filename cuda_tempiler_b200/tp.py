@@ -165,11 +165,14 @@ class PeerAllReduce:
         self._recv_ptrs = (C.c_void_p * self.tp)(*rp)
         self._flag_ptrs = (C.c_void_p * self.tp)(*fp)
         self.epoch = 0
+        # the device-side epoch of the graph-capturable form (``device_epoch=True`` calls)
+        self._epoch_ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
 
     def __call__(self, y: torch.Tensor) -> torch.Tensor:
-        """In place: y <- sum of y over the ranks."""
+        """In place: y <- sum of y over the ranks.  The epoch lives on the device, so the call
+        can be captured in a CUDA graph (``MLPGraph``); all ranks make every call in step."""
         import torch.distributed as dist
 
         from . import _lib
@@ -177,11 +180,11 @@ class PeerAllReduce:
         if y.dtype != torch.float16 or not y.is_contiguous() or n % 8 or n > self.cap:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
             return y
-        self.epoch += 1
-        rc = self._lib.tempo_sm100_allreduce_oneshot(
+        rc = self._lib.tempo_sm100_allreduce_oneshot_dev(
             y.data_ptr(), y.data_ptr(), n, self.cap, self._recv_ptrs, self._flag_ptrs, self.tp,
-            self.rank, self.epoch, self.ctas, torch.cuda.current_stream(self.device).cuda_stream)
-        _lib.check(rc, "tempo_sm100_allreduce_oneshot")
+            self.rank, self._epoch_ctr.data_ptr(), self.ctas,
+            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "tempo_sm100_allreduce_oneshot_dev")
         return y
 
     def close(self):
@@ -219,3 +222,33 @@ def mlp_forward(x: torch.Tensor, shard: MLPShard, group=None, gemm=None, swiglu=
         if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
+
+
+class MLPGraph:
+    """One rank's MLP forward for a fixed M captured in a CUDA graph and replayed: at decode
+    sizes the forward is a handful of short kernels (two GEMVs, SwiGLU, the all-reduce) whose
+    host launch cost exceeds their device time once the weights are split over several GPUs,
+    so each forward is one graph launch instead.  The all-reduce inside the graph is NCCL's
+    (capturable) by default, or ``all_reduce=PeerAllReduce(...)``, the library's one-shot peer
+    all-reduce, which keeps its epoch on the device and so replays correctly.  ``__call__(x)``
+    copies x into the graph's input buffer, replays, and returns the
+    graph's output buffer (overwritten by the next call)."""
+
+    def __init__(self, shard: MLPShard, M: int, H: int, device, group=None, warmup: int = 2,
+                 all_reduce=True):
+        self.x = torch.zeros(M, H, dtype=torch.float16, device=device)
+        self.stream = torch.cuda.Stream(device)
+        self.stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(self.stream):
+            # warm-up on the capture stream: cached workspaces and tensor maps exist before capture
+            for _ in range(warmup):
+                mlp_forward(self.x, shard, group, all_reduce=all_reduce)
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.y = mlp_forward(self.x, shard, group, all_reduce=all_reduce)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x)
+        self.graph.replay()
+        return self.y

@@ -171,6 +171,14 @@ int tempo_sm100_allreduce_oneshot_timed(const void* src, void* dst, long long n,
                                         unsigned epoch, int ctas, unsigned long long wait_ns,
                                         void* stream);
 
+/* The same with the epoch kept on the device: epoch_ctr is this rank's own buffer of two
+ * uint32 (8-byte aligned, zeroed once), which the kernel reads and advances itself, so the
+ * call can be captured in a CUDA graph and replayed (every rank must replay in step).  Do not
+ * mix it with explicit-epoch calls on the same buffers. */
+int tempo_sm100_allreduce_oneshot_dev(const void* src, void* dst, long long n, long long cap,
+                                      void* const* recv, void* const* flags, int tp, int rank,
+                                      void* epoch_ctr, int ctas, void* stream);
+
 /* Device status written by bounded waits inside the kernels: out[0] = 0 ok / 1 timeout,
  * out[1] = role that gave up, out[2] = block.  reset != 0 clears it.  Synchronises the
  * current device. */

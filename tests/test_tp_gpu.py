@@ -260,3 +260,69 @@ def test_peer_allreduce_two_ranks():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert ok and st == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("M", [1, 16, 1024])
+def test_mlp_graph_replay_matches_eager(dev, M):
+    """The MLP forward captured in a CUDA graph gives the eager forward's result, twice in a
+    row with different inputs (the graph reads its input buffer on every replay)."""
+    from cuda_tempiler_b200 import tp
+    x, wg, wu, wd, sg, su, sd = _mlp_inputs(M, 512, 1024, dev)
+    sh = tp.shard_mlp(wg, wu, wd, 1, 0, sg, su, sd)
+    mg = tp.MLPGraph(sh, M, 512, dev)
+    for seed in (1, 2):
+        xs = _mlp_inputs(M, 512, 1024, dev, seed=seed)[0]
+        y = mg(xs).clone()
+        ref = tp.mlp_forward(xs, sh)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+        assert O.rel_l2(y.float().cpu().numpy(), _oracle_mlp(xs, wg, wu, wd, sg, su, sd)) <= O.GATE_REL_L2
+
+
+def _graph_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    from cuda_tempiler_b200 import tp
+    x, wg, wu, wd, sg, su, sd = _mlp_inputs(4, 512, 1024, torch.device("cuda", rank))
+    sh = tp.shard_mlp(wg, wu, wd, world, rank, sg, su, sd)
+    mg = tp.MLPGraph(sh, 4, 512, torch.device("cuda", rank))
+    y = mg(x).clone()
+    par = tp.PeerAllReduce(16 * 512)
+    mp_ = tp.MLPGraph(sh, 4, 512, torch.device("cuda", rank), all_reduce=par)
+    y2 = mp_(x).clone()
+    y3 = mp_(x).clone()  # a second replay: a new device-side epoch
+    torch.cuda.synchronize()
+    del mg, mp_
+    torch.cuda.synchronize()
+    if rank == 0:
+        q.put((y.float().cpu().numpy(), y2.float().cpu().numpy(), y3.float().cpu().numpy(),
+               _oracle_mlp(x, wg, wu, wd, sg, su, sd)))
+    par.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_mlp_graph_two_ranks():
+    """The graph-captured forward on 2 GPUs with NCCL's all-reduce inside the graph, and with
+    the peer one-shot all-reduce (device-side epoch) inside it, replayed twice."""
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_graph_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    y, y2, y3, ref = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for got in (y, y2, y3):
+        assert O.rel_l2(got, ref) <= O.GATE_REL_L2
