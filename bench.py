@@ -268,11 +268,13 @@ def tp_mlp_block(dev, world, rank, barrier):
         try:
             par = tp.PeerAllReduce(16 * H)
             probe = torch.randn(16 * H, generator=g, device=dev).half()
-            want = probe.clone()
+            # against an fp32 sum: the one-shot kernel adds in fp32 and rounds once, whereas
+            # NCCL's fp16 ring rounds at every hop (at 8 ranks by more than the tolerance)
+            want = probe.float()
             dist.all_reduce(want)
             par(probe)
             torch.cuda.synchronize()
-            good = float(torch.allclose(probe.float(), want.float(), rtol=2e-3, atol=2e-3))
+            good = float(torch.allclose(probe.float(), want, rtol=2e-3, atol=2e-3))
         except Exception as e:  # reported, and every rank then keeps NCCL
             print(f"peer all-reduce unavailable: {e}", file=sys.stderr)
         ok = torch.tensor([good], device=dev)
