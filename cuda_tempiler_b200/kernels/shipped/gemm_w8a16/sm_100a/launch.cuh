@@ -11,7 +11,7 @@
 //                                         zero uint8 [K/group][N]:  w = (q - z[g][n]) * s[g][n]
 //
 // The group-wise scale and zero arrays are GPTQ's own orientation (its scales array and the
-// byte view of its qzeros, used as they are).  From M = 512 on, given a workspace of at least
+// byte view of its qzeros, used as they are).  From M = 1024 on, given a workspace of at least
 // N * K * 2 bytes, the weights are first expanded to fp16 in the workspace and the fp16 2-CTA
 // tiles run on the copy (plan() reports expand = 1 and the bytes it wants).
 #pragma once
