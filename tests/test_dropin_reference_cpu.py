@@ -1,8 +1,8 @@
 """Drop-in proof: the sm100 plugin directory, placed into a copy of the reference tree as
 tempo/plugins/sm100/, is loaded and driven by the reference's own unmodified pipeline
 (``python3 -m tempo.cli plugins/selftest/space/emit``) and the kernel it emits compiles for
-sm_100a.  Runs only where the reference checkout exists (this is a CPU test; nothing on the GPU
-side reads the reference)."""
+sm_100a.  Runs when TEMPO_REFERENCE names a reference checkout (this is a CPU test; nothing on
+the GPU side reads the reference)."""
 import os
 import shutil
 import subprocess
@@ -10,12 +10,12 @@ import sys
 
 import pytest
 
-REF = os.environ.get("TEMPO_REFERENCE", "/root/reference")
+REF = os.environ.get("TEMPO_REFERENCE", "")
 PLUGIN = os.path.join(os.path.dirname(os.path.dirname(__file__)), "cuda_tempiler_b200", "tempo",
                       "plugins", "sm100")
 
-pytestmark = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "tempo")),
-                                reason="reference tree not available")
+pytestmark = pytest.mark.skipif(not REF or not os.path.isdir(os.path.join(REF, "tempo")),
+                                reason="set TEMPO_REFERENCE to a reference checkout")
 
 
 @pytest.fixture(scope="module")
