@@ -127,8 +127,7 @@ int tempo_sm100_gemm_hyperform_cg(int weight_kind, const void* A, const void* W,
                             group_size)) {
     return cudaErrorInvalidConfiguration;
   }
-  // W8A16 pair tiles take whole tiles only (no split tail)
-  Hyper h{bn, 0, (splits > 1 && weight_kind == 0) ? 2 : 1, group_m < 1 ? 1 : group_m, max_ctas};
+  Hyper h{bn, 0, splits > 1 ? 2 : 1, group_m < 1 ? 1 : group_m, max_ctas};
   h.cta_group = 2;
   Problem pr{weight_kind, A, W, scale, zero, C, M, N, K, lda, ldw, ldc, group_size, ws, ws_bytes};
   return run(pr, h, static_cast<cudaStream_t>(stream));

@@ -2252,8 +2252,11 @@ __global__ void __launch_bounds__(PairCfg<BN>::THREADS, 1)
 // Warps: 0 A producer, 1 MMA issuer (leader) / TMEM owner, 2-5 epilogue, 6 raw producer,
 // 7 .. 6 + NS * WPG dequant (WPG warps own each slot, so every wait on a slot's barriers is
 // made by its single owner group, in order, and never sees an older phase).  Per-channel scales
-// are applied in the epilogue; group-wise scale and zero point in the dequant.  Whole tiles
-// only (no split tail), no SwiGLU.
+// are applied in the epilogue; group-wise scale and zero point in the dequant.  The tiles of a
+// ragged last wave -- or all tiles, when there are fewer tiles than clusters (the narrow-N
+// shapes at M = 256) -- may run as k-slices (pair_plan's split tail), their fp32 partials
+// summed in k order by the last slice to arrive, which applies the per-channel scale.  No
+// SwiGLU.
 // ---------------------------------------------------------------------------------------------
 template <int BN_>
 struct PairW8Cfg {
@@ -2302,6 +2305,7 @@ __global__ void __launch_bounds__(PairW8Cfg<BN>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -2550,6 +2554,108 @@ __global__ void __launch_bounds__(PairW8Cfg<BN>::THREADS, 1)
       const uint32_t t_acc = t_lane + buf * Cfg::ACC_STRIDE;
       const int q0 = tq * BN;
       const int row0 = tp * 256 + (int)rank * 128 + quad * 32;
+      if (sg.contrib > 1 && (args.ws == nullptr || args.counters == nullptr)) {
+        // a split unit without workspace is a host-side bug: report it instead of faulting
+        if (lane == 0 && atomicCAS(&g_status[0], 0, 2) == 0) {
+          g_status[1] = 16;
+          g_status[2] = blockIdx.x;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+        continue;
+      }
+      if (sg.contrib > 1) {
+        // Tail k-slice: this CTA's 128 x BN fp32 partial goes to slot (slice, t), laid out
+        // [32-column chunk][row][32] so each thread writes and reads its row's 128 contiguous
+        // bytes per chunk as float4s.  The last of the tile's k-slices to arrive keeps its own
+        // accumulator in TMEM, adds the other slots in k order (deterministic) and writes C.
+        const int skt = sg.t;
+        const long long slice = (long long)128 * BN;
+        const long long slot_stride = 2LL * args.sk_tiles * slice;  // next k-slice, same tile
+        const float* base = args.ws + ((long long)skt * 2 + rank) * slice;
+        const int row = quad * 32 + lane;
+        float4* part = reinterpret_cast<float4*>(const_cast<float*>(base) + sg.slot * slot_stride);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float f[32];
+          acc_chunk<32, 1, BN>(t_acc, c, f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(part + (c * 128 + row) * 8 + q,
+                   make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]));
+        }
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 64) {
+          int* ctr = args.counters + skt * 2 + rank;
+          const int old = atomicAdd(ctr, 1);
+          const int last = old == sg.contrib - 1;
+          if (last) atomicExch(ctr, 0);  // ready for the next call
+          *last_flag = last;
+        }
+        named_barrier_sync(1, 128);
+        const bool last = *last_flag != 0;
+        if (!last) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+          continue;
+        }
+        __threadfence();
+        const int p = row0 + lane;
+        const int S = sg.contrib;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float acc[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          // slots in k order, one at a time (the wide CTA has fewer registers per thread
+          // than the fp16 kernel); this CTA's own slot comes from TMEM
+          for (int j = 0; j < S; ++j) {
+            if (j == sg.slot) {
+              float f[32];
+              acc_chunk<32, 1, BN>(t_acc, c, f);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[i] += f[i];
+            } else {
+              const float4* src = reinterpret_cast<const float4*>(base + j * slot_stride) +
+                                  (c * 128 + row) * 8;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 x = __ldcg(src + q);
+                acc[4 * q] += x.x;
+                acc[4 * q + 1] += x.y;
+                acc[4 * q + 2] += x.z;
+                acc[4 * q + 3] += x.w;
+              }
+            }
+          }
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
+          }
+          if (p >= args.rows_p) continue;
+#pragma unroll
+          for (int i0 = 0; i0 < 32; i0 += 8) {
+            const int q = q0 + c * 32 + i0;
+            if (q >= args.rows_q) break;
+            if (WQ == kWInt8PerChannel) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                acc[i0 + j] *= q + j < args.rows_q ? __half2float(__ldg(args.scale + q + j)) : 0.f;
+            }
+            uint4 w;
+            w.x = pack_half2(acc[i0 + 0], acc[i0 + 1]);
+            w.y = pack_half2(acc[i0 + 2], acc[i0 + 3]);
+            w.z = pack_half2(acc[i0 + 4], acc[i0 + 5]);
+            w.w = pack_half2(acc[i0 + 6], acc[i0 + 7]);
+            *reinterpret_cast<uint4*>(args.C + (long long)p * args.ldc + q) = w;
+          }
+        }
+        continue;
+      }
       const int live_cols = args.rows_q - q0;
       const bool rows_live = row0 < args.rows_p;
       const int nchunk = live_cols >= BN ? BN / 32 : (live_cols + 31) / 32;

@@ -588,7 +588,8 @@ cudaError_t launch_pair(const Problem& pr, const Hyper& h, cudaStream_t st) {
                    a);
 }
 
-// W8A16 2-CTA launch (k_gemm_sm100_pair_w8): whole tiles, persistent clusters.
+// W8A16 2-CTA launch (k_gemm_sm100_pair_w8): persistent clusters; h.splits > 1 allows the
+// split tail of pair_plan (given the workspace it needs).
 template <int BN, int WQ>
 cudaError_t launch_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
   using Cfg = PairW8Cfg<BN>;
@@ -609,7 +610,8 @@ cudaError_t launch_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
   if (pr.wkind != WQ || h.swap) return cudaErrorInvalidConfiguration;
   if (WQ == kWUint8Group && (pr.group <= 0 || pr.group % Cfg::BK || pr.K % pr.group || pr.N % 16))
     return cudaErrorInvalidConfiguration;
-  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas, false, 0);
+  const PairPlan pl = pair_plan(pr.M, pr.N, pr.K, BN, dev_info(dev).sms, h.max_ctas,
+                                h.splits > 1, pr.ws ? pr.ws_bytes : 0);
   GemmArgs a{};
   a.rows_p = pr.M;
   a.rows_q = pr.N;
@@ -627,7 +629,15 @@ cudaError_t launch_pair_w8(const Problem& pr, const Hyper& h, cudaStream_t st) {
   a.zero = static_cast<const uint8_t*>(pr.zero);
   a.group_size = pr.group > 0 ? pr.group : 1;
   a.groups_per_row = pr.group > 0 ? pr.K / pr.group : 1;
-  a.sk_tile0 = pl.sk_tile0;  // == tiles: no split tail
+  a.sk_tile0 = pl.sk_tile0;
+  a.sk_tiles = pl.sk_tiles;
+  a.sk_splits = pl.sk_splits;
+  if (pl.sk_splits > 0) {
+    if (!pr.ws || pr.ws_bytes < pl.ws_bytes) return cudaErrorInvalidValue;
+    a.counters = static_cast<int*>(pr.ws);
+    a.ws = reinterpret_cast<float*>(pr.ws_parts ? static_cast<char*>(pr.ws_parts)
+                                                : static_cast<char*>(pr.ws) + kCounterBytes);
+  }
   CUtensorMap mA, mW, mC, mS, mZ;
   std::memset(&mA, 0, sizeof(mA));
   std::memset(&mW, 0, sizeof(mW));
@@ -711,8 +721,7 @@ int choose_pair_bn(int M, int N, int K, int sms, int bn_max, size_t ws_bytes, in
   for (int i = 0; i < nw; ++i) {
     const int bn = widths[i];
     if (bn > bn_max) continue;
-    // W8A16 pair tiles run whole tiles only (no split tail)
-    const PairPlan pl = pair_plan(M, N, K, bn, sms, 0, wkind == 0, ws_bytes);
+    const PairPlan pl = pair_plan(M, N, K, bn, sms, 0, true, ws_bytes);
     const double c = pl.cost * bn / 256.0 / eff[i];
     if (best == 0 || c < best_c) {
       best = bn;
@@ -861,7 +870,7 @@ bool select_hyper(int wkind, const LadderRow& r, int M, int N, int K, size_t ws_
   }
   if (h.cta_group == 2) {  // pair tiles: width and (fp16) split tail by the wave model
     h.bn = choose_pair_bn(M, N, K, sms, h.bn, ws_bytes, wkind);
-    h.splits = wkind == 0 ? 2 : 1;
+    h.splits = 2;  // the split tail of pair_plan is allowed
     if (wkind == kWUint8Group && (N % 16)) return false;  // scale/zero rows by TMA
     return h.bn != 0;
   }

@@ -193,3 +193,26 @@ def test_pair_tiles_w8(dev, bn, M, N, K):
             A, W, bn=bn, swap=False, cta_group=2, scale=s, zero=z, group_size=G, out=C))
     assert r1 <= TOL and r2 <= TOL, (r1, r2)
     assert ops.device_status() == [0, 0, 0, 0]
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("M,N,K", [(256, 1024, 8192), (300, 784, 4096), (256, 5120, 17408)])
+def test_pair_tiles_w8_split_tail(dev, bn, M, N, K):
+    """W8A16 2-CTA tiles with the split tail (fewer tiles than clusters: every tile cut into
+    k-slices, fp32 partials summed in k order by the last slice, per-channel scale applied
+    there): gate passed, bit-identical run to run."""
+    from cuda_tempiler_b200 import ops
+    f = lambda A, W, s, C: ops.gemm_hyperform(A, W, bn=bn, swap=False, cta_group=2, splits=2,
+                                              scale=s, out=C)
+    assert _pc(M, N, K, f) <= TOL
+    a, q, s = O.inputs_w8_per_channel(M, N, K, 2)
+    A, Q, S = (torch.from_numpy(x).cuda() for x in (a, q, s))
+    c1 = ops.gemm_hyperform(A, Q, bn=bn, swap=False, cta_group=2, splits=2, scale=S)
+    c2 = ops.gemm_hyperform(A, Q, bn=bn, swap=False, cta_group=2, splits=2, scale=S)
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2)
+    if N % 16 == 0:
+        r = _grp(M, N, K, lambda A, W, s, z, G, C: ops.gemm_hyperform(
+            A, W, bn=bn, swap=False, cta_group=2, splits=2, scale=s, zero=z, group_size=G, out=C))
+        assert r <= TOL
+    assert ops.device_status() == [0, 0, 0, 0]
