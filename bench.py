@@ -752,11 +752,18 @@ def main():
     t = dom_ms * 1e-3
     traffic = load_traffic().get(f"{x['name']}_M{x['M']}")
     if fl / (peaks["tc"] * 1e12) >= by / (peaks["hbm"] * 1e9):
-        roof = {"bound": "tensor", "achieved": fl / t / 1e12, "peak": peaks["tc"],
+        # a timed region of a quarter second or more runs under the power cap (clocks settle
+        # below max): the sustained GEMM peak is the denominator then, the burst peak below
+        long_run = ms_total >= 250.0
+        pk = peaks["tc_sus"] if long_run else peaks["tc"]
+        roof = {"bound": "tensor", "achieved": fl / t / 1e12, "peak": pk,
                 "unit": "TFLOP/s", "kernel": f"{x['name']} M={x['M']} N={x['N']} K={x['K']}",
                 "algorithmic": f"2MNK = {fl} FLOP per launch",
-                "peak_source": f"{peaks['src']} bf16_tflops (burst: the timed region is "
-                               f"{ms_total:.0f} ms, not a seconds-long run)",
+                "peak_source": (f"{peaks['src']} bf16_tflops_sustained (the timed region is "
+                                f"{ms_total:.0f} ms, under the power cap)" if long_run else
+                                f"{peaks['src']} bf16_tflops (burst: the timed region is "
+                                f"{ms_total:.0f} ms, not a seconds-long run)"),
+                "frac_of_burst": fl / t / 1e12 / peaks["tc"],
                 "frac_of_sustained": fl / t / 1e12 / peaks["tc_sus"]}
     else:
         roof = {"bound": "hbm", "achieved": by / t / 1e9, "peak": peaks["hbm"], "unit": "GB/s",
