@@ -429,20 +429,27 @@ size_t expand_ws_bytes(int N, int K) { return ((size_t)N * K * 2 + 255) / 256 * 
 // start: a workspace reused by a later split-K launch must still hold zeroed counters there).
 constexpr size_t kExpandOffset = kCounterBytes;
 
-cudaError_t launch_expand(const Problem& pr, __half* out, cudaStream_t st) {
-  const long long n = (long long)pr.N * (pr.K / 16);
+// Rows [n0, n0 + rows) of the weights expanded into out (rows x K, dense); wait as in
+// k_expand_w8.
+cudaError_t launch_expand_rows(const Problem& pr, int n0, int rows, __half* out, bool wait,
+                               cudaStream_t st) {
+  const long long n = (long long)rows * (pr.K / 16);
   const unsigned grid = (unsigned)((n + 255) / 256);
-  const uint8_t* W = static_cast<const uint8_t*>(pr.W);
-  const __half* sc = static_cast<const __half*>(pr.scale);
-  const uint8_t* z = static_cast<const uint8_t*>(pr.zero);
+  const uint8_t* W = static_cast<const uint8_t*>(pr.W) + (long long)n0 * pr.ldw;
+  const __half* sc = static_cast<const __half*>(pr.scale) + n0;
+  const uint8_t* z = pr.zero ? static_cast<const uint8_t*>(pr.zero) + n0 : nullptr;
   const int g = pr.group > 0 ? pr.group : 16;
   if (pr.wkind == kWInt8PerChannel)
     return launch_ex(k_expand_w8<kWInt8PerChannel>, dim3(grid), dim3(256), 0, st, 1, W, sc, z,
-                     out, pr.N, pr.K, (long long)pr.ldw, g);
+                     out, rows, pr.K, (long long)pr.ldw, g, pr.N, wait ? 1 : 0);
   if (pr.wkind == kWUint8Group)
     return launch_ex(k_expand_w8<kWUint8Group>, dim3(grid), dim3(256), 0, st, 1, W, sc, z, out,
-                     pr.N, pr.K, (long long)pr.ldw, g);
+                     rows, pr.K, (long long)pr.ldw, g, pr.N, wait ? 1 : 0);
   return cudaErrorInvalidConfiguration;
+}
+
+cudaError_t launch_expand(const Problem& pr, __half* out, cudaStream_t st) {
+  return launch_expand_rows(pr, 0, pr.N, out, true, st);
 }
 
 using LaunchFn = cudaError_t (*)(const Problem&, const Hyper&, cudaStream_t);

@@ -932,22 +932,25 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
 // (q - z) * s group-wise), 16 k per thread: 16 bytes in, 32 bytes out, streamed once.  For
 // prefill-sized M the tensor-core kernel then runs on fp16 weights at the full 2-CTA rate;
 // the pass costs 3 bytes per weight of HBM traffic, small against the GEMM at such M.
+// ldsz: row stride of the group-wise scale / zero arrays [K/g][ldsz].  wait = 0 skips the
+// programmatic-launch wait: the launch that expands a later slice of the weights reads only the
+// weights, never the preceding GEMM's output, so it may run beside that GEMM.
 template <int WQ>
 __global__ void __launch_bounds__(256)
     k_expand_w8(const uint8_t* __restrict__ W, const __half* __restrict__ scale,
                 const uint8_t* __restrict__ zero, __half* __restrict__ out, int N, int K,
-                long long ldw, int group) {
+                long long ldw, int group, int ldsz, int wait) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = K / 16;
   if (i >= (long long)N * per_row) return;
-  pdl_wait();
+  if (wait) pdl_wait();
   pdl_launch_dependents();
   const int n = (int)(i / per_row);
   const int k0 = (int)(i - (long long)n * per_row) * 16;
   const uint4 x = ld_stream(W + (long long)n * ldw + k0);
   __half2 zb = __float2half2_rn(0.f), s2 = zb;
   if (WQ == kWUint8Group) {
-    const long long gi = (long long)(k0 / group) * N + n;
+    const long long gi = (long long)(k0 / group) * ldsz + n;
     zb = __half2half2(__ushort_as_half((unsigned short)(0x6400u | __ldg(zero + gi))));
     s2 = __half2half2(__ldg(scale + gi));
   }
