@@ -86,9 +86,10 @@ int tempo_sm100_gemm_hyperform(int weight_kind, const void* A, const void* W, co
                                int ldc, int group_size, int bn, int swap, int splits, int group_m,
                                int max_ctas, void* ws, size_t ws_bytes, void* stream);
 
-/* As tempo_sm100_gemm_hyperform with the cluster axis: cta_group 2 runs fp16 prefill tiles of
- * 256 x bn (bn 128 or 256) on 2-CTA clusters with tcgen05.mma.cta_group::2 (weight_kind 0,
- * swap 0).  There splits 1 = one cluster per tile; splits > 1 lets a ragged last wave run as
+/* As tempo_sm100_gemm_hyperform with the cluster axis: cta_group 2 runs prefill tiles of
+ * 256 x bn on 2-CTA clusters with tcgen05.mma.cta_group::2 (swap 0): fp16 weights with bn
+ * 128..256 step 32, 8-bit weights (dequantised in shared memory by each CTA) with bn 128 or
+ * 256.  There splits 1 = one cluster per tile; splits > 1 lets a ragged last wave run as
  * a split tail (its tiles cut into k-slices, reduced in k order by the last slice; needs up to
  * 65536 + 3 * P * 2 * 128 * bn * 4 bytes of workspace for P = SMs / 2 clusters, else the
  * launch stays data-parallel).  cta_group 1 is tempo_sm100_gemm_hyperform. */
